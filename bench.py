@@ -1,0 +1,318 @@
+"""Benchmark: erode + dilate forward + backward throughput on B200.
+
+Workload (the separable flat-rectangle configuration the headline metric is quoted on):
+x = rand(32, 64, 512, 512) float32, grad_output = randn_like(x), flat square(15) structuring element,
+REFLECT border; one step = dilation(x) and erosion(x), each forward + backward, through the public
+API (``serron_b200.dilation`` / ``erosion`` + autograd).  Inputs (2.1 GB each) are far larger than L2,
+so no flush is needed between steps.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1: one process per GPU (torchrun); every rank runs the same per-GPU workload with its own seed
+(weak scaling, no collective on the data path); time = max over ranks of CUDA-event time.
+``--impl reference`` times the reference's own CPU implementation (compiled from its sources into
+``oracle/_ref``; the oracle port when that library is absent) on a bounded slice of the workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+import torch  # noqa: E402
+
+SHAPE = (32, 64, 512, 512)
+K = 15
+BORDER_NAME = "reflect"
+METRIC = "output Gpix/s erode+dilate fwd+bwd per GPU at 1/2/4/8 B200; % of HBM/min-max roofline"
+WORKLOAD = "flat separable: dilation+erosion of x(32,64,512,512) fp32 uniform[0,1), square(15), REFLECT, fwd+bwd"
+PRIMS = 2  # primitive calls per step
+# algorithmic HBM bytes per output pixel of each kernel (fp32 value 4 B, winner record 1 B)
+FWD_BYTES_PER_PX = 4 + 4 + 1  # read x, write y, write winners
+BWD_BYTES_PER_PX = 4 + 1 + 4  # read grad_output, read winners, write grad_input
+# per-launch DRAM traffic of each kernel at the full workload, from the ncu captures summarised in
+# profiles/ (None until captured)
+NCU_TRAFFIC_BYTES = {"sep_fwd": None, "sep_gather": None}
+CPU_SAMPLE = (1, 4, 512, 512)  # slice of the workload the CPU baseline times (scaled linearly in pixels)
+
+
+def _peaks() -> tuple[float, str]:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clocks and throttle reasons with nvidia-smi while the timed region runs."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int) -> None:
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+        self.reader = None
+
+    def start(self) -> None:
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.reader = threading.Thread(target=self._read, daemon=True)
+        self.reader.start()
+
+    def _read(self) -> None:
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.reader is not None:
+            self.reader.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower() == "active":
+                    reasons.add(name)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def _dist() -> tuple[int, int, int]:
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _cpu_baseline(steps: int) -> dict:
+    """The reference's CPU path on a slice, all host threads; Gpix/s scaled by pixels."""
+    import oracle
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(0)
+    x = torch.rand(*CPU_SAMPLE, generator=g)
+    go = torch.randn(*CPU_SAMPLE, generator=g)
+    w = torch.zeros(K, K)
+    ref = oracle.reference_ops()
+    kind = "reference" if ref is not None else "port"
+
+    def step() -> None:
+        if ref is not None:
+            for fwd, bwd in ((ref.dilate, ref.dilate_backward), (ref.erode, ref.erode_backward)):
+                fwd(x, w, 0, True, 0)
+                bwd(go, x, w, 0, True, False, 0)
+        else:
+            for op in (oracle.DILATE, oracle.ERODE):
+                oracle.forward(op, x, w, 0, separable=True)
+                oracle.backward(op, go, x, w, 0, separable=True, need_kernel_grad=False)
+
+    step()
+    t0 = time.perf_counter()
+    for _ in range(steps):
+        step()
+    dt = (time.perf_counter() - t0) / steps
+    px = CPU_SAMPLE[0] * CPU_SAMPLE[1] * CPU_SAMPLE[2] * CPU_SAMPLE[3]
+    return {"value": px * PRIMS / dt / 1e9, "unit": "Gpix/s", "cores": torch.get_num_threads(), "kind": kind,
+            "sample": f"x{CPU_SAMPLE} (one 4-channel slice of the 32x64 batch), dilation+erosion fwd+bwd, "
+                      f"{steps} step(s) after 1 warm-up, {dt:.2f} s/step; Gpix/s scales linearly in pixels",
+            "ms_per_step_sample": dt * 1e3}
+
+
+def run_reference(args) -> None:
+    world, rank, _ = _dist()
+    if rank != 0:
+        return
+    steps = max(1, min(args.steps, 3))
+    base = _cpu_baseline(steps)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "Gpix/s", "n_gpus": args.gpus,
+        "steps": steps, "warmup": 1, "ms_per_step": base["ms_per_step_sample"], "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample": list(CPU_SAMPLE)},
+        "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
+        "e2e": {"value": base["value"], "unit": "Gpix/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    world, rank, local = _dist()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py: needs a CUDA device")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    import serron_b200 as serron
+    from serron_b200 import _lib
+
+    _lib.load()
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.rand(*SHAPE, device=dev, generator=gen).requires_grad_(True)
+    go = torch.randn(*SHAPE, device=dev, generator=gen)
+    k = serron.structuring_element.square(K, device=dev)
+    border = serron.BorderMode.REFLECT
+    px = SHAPE[0] * SHAPE[1] * SHAPE[2] * SHAPE[3]
+
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(5)]
+    kernel_ms = {"sep_fwd": [], "sep_gather": []}
+
+    def step(record: bool) -> None:
+        i = 0
+        for fn in (serron.dilation, serron.erosion):
+            if record:
+                ev[i].record()
+            y = fn(x, k, border=border)
+            if record:
+                ev[i + 1].record()
+            (gx,) = torch.autograd.grad(y, x, go)
+            i += 2
+        if record:
+            ev[4].record()
+
+    for _ in range(args.warmup):
+        step(False)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    clocks = ClockSampler(local) if rank == 0 else None
+    if clocks:
+        clocks.start()
+        time.sleep(0.3)
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(args.steps):
+        step(True)
+        torch.cuda.synchronize()
+        kernel_ms["sep_fwd"] += [ev[0].elapsed_time(ev[1]), ev[2].elapsed_time(ev[3])]
+        kernel_ms["sep_gather"] += [ev[1].elapsed_time(ev[2]), ev[3].elapsed_time(ev[4])]
+    stop.record()
+    torch.cuda.synchronize()
+    clock_info = clocks.stop() if clocks else None
+    elapsed = start.elapsed_time(stop)
+    t = torch.tensor([elapsed], device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        dist.barrier()
+    ms_per_step = float(t.item()) / args.steps
+    value = px * PRIMS * world / (ms_per_step * 1e-3) / 1e9
+
+    # end to end through the public API with host buffers: H2D of the step's inputs from pinned memory,
+    # both ops forward + backward, D2H of both outputs and both input gradients
+    x_host = x.detach().cpu().pin_memory()
+    go_host = go.cpu().pin_memory()
+    outs = [torch.empty(SHAPE, dtype=torch.float32).pin_memory() for _ in range(4)]
+
+    def e2e_step() -> None:
+        xd = x_host.to(dev, non_blocking=True).requires_grad_(True)
+        god = go_host.to(dev, non_blocking=True)
+        j = 0
+        for fn in (serron.dilation, serron.erosion):
+            y = fn(xd, k, border=border)
+            (gx,) = torch.autograd.grad(y, xd, god)
+            outs[j].copy_(y.detach(), non_blocking=True)
+            outs[j + 1].copy_(gx, non_blocking=True)
+            j += 2
+
+    e2e_steps = max(1, min(args.steps, 3))
+    e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    te = torch.tensor([e0.elapsed_time(e1) / e2e_steps], device=dev)
+    if world > 1:
+        dist.all_reduce(te, op=dist.ReduceOp.MAX)
+    e2e_value = px * PRIMS * world / (float(te.item()) * 1e-3) / 1e9
+
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        kernels = {}
+        for name, per_px in (("sep_fwd", FWD_BYTES_PER_PX), ("sep_gather", BWD_BYTES_PER_PX)):
+            avg = statistics.mean(kernel_ms[name])
+            achieved = px * per_px / (avg * 1e-3) / 1e9
+            traffic = NCU_TRAFFIC_BYTES[name]
+            kernels[name] = {"ms": avg, "achieved": achieved, "algorithmic_bytes": px * per_px,
+                             "frac": achieved / peak, "traffic": traffic}
+        dominant = max(kernels, key=lambda n: kernels[n]["ms"])
+        dk = kernels[dominant]
+        line = {
+            "metric": METRIC, "value": value, "unit": "Gpix/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "per_gpu_batch": list(SHAPE), "se": "square(15) flat",
+                       "border": BORDER_NAME, "l2": "inputs 2.1 GB >> 126 MB L2, no flush needed"},
+            "roofline": {"bound": "hbm", "kernel": dominant, "achieved": dk["achieved"], "peak": peak,
+                         "unit": "GB/s", "frac": dk["frac"], "traffic": dk["traffic"], "peak_source": peak_kind},
+            "kernels": kernels,
+            "e2e": {"value": e2e_value, "unit": "Gpix/s", "h2d_bytes_per_step": 2 * px * 4,
+                    "d2h_bytes_per_step": 4 * px * 4},
+            "gpu_launches": 4 * args.steps,
+            "clocks": clock_info,
+        }
+        if world == 1:
+            line["cpu_baseline"] = {k_: v for k_, v in _cpu_baseline(1).items() if k_ != "ms_per_step_sample"}
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main() -> None:
+    p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=10)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    args = p.parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,872 @@
+// C ABI of the sm_100a morphology library: validation, algorithm resolution, buffer sizing and kernel
+// launches.  Declarations and the contract of every entry point: include/serron_b200.h.
+//
+// Host-side behaviour follows the reference's CUDA operators (vhrabar/serron 0.6.0, packages/serron/):
+// validation and messages csrc/gpu/morphology/operators.cpp:153-190 and backward.cpp:154-194,
+// algorithm resolution csrc/gpu/morphology/algorithm.h:103-137, thresholds
+// csrc/gpu/morphology/thresholds.h:46-71 with the SERRON_SEPARABLE_MIN_K override of
+// csrc/gpu/morphology/separable.h:104-116, flatness read-back separable.h:150-169.
+#include "serron_b200.h"
+
+#include "common.cuh"
+#include "direct.cuh"
+#include "recon.cuh"
+#include "segrad.cuh"
+#include "separable.cuh"
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <sstream>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <vector>
+
+namespace serron {
+namespace {
+
+thread_local std::string g_last_error;
+
+struct Failure {
+    int code;
+    std::string message;
+};
+
+template <typename... Args>
+std::string concat(const Args&... args) {
+    std::ostringstream oss;
+    ((oss << args), ...);
+    return oss.str();
+}
+
+#define SB_CHECK(cond, ...)                                                  \
+    do {                                                                     \
+        if (!(cond)) throw Failure{SERRON_ERR_INVALID, concat(__VA_ARGS__)}; \
+    } while (0)
+
+#define SB_CUDA(expr)                                                                                         \
+    do {                                                                                                      \
+        const cudaError_t err_ = (expr);                                                                      \
+        if (err_ != cudaSuccess)                                                                              \
+            throw Failure{SERRON_ERR_CUDA, concat("serron: CUDA error ", cudaGetErrorName(err_), ": ",      \
+                                                  cudaGetErrorString(err_), " (", #expr, ")")};              \
+    } while (0)
+
+template <typename F>
+int guarded(F&& f) {
+    try {
+        f();
+        return SERRON_OK;
+    } catch (const Failure& e) {
+        g_last_error = e.message;
+        return e.code;
+    } catch (const std::exception& e) {
+        g_last_error = e.what();
+        return SERRON_ERR_INVALID;
+    }
+}
+
+// Makes `device` current for the scope of a call and restores the previous device.
+struct DeviceScope {
+    int previous = -1;
+    explicit DeviceScope(int device) {
+        if (cudaGetDevice(&previous) != cudaSuccess) previous = -1;
+        cudaGetLastError();
+        if (previous != device) SB_CUDA(cudaSetDevice(device));
+    }
+    ~DeviceScope() {
+        int now = -1;
+        if (previous >= 0 && cudaGetDevice(&now) == cudaSuccess && now != previous) cudaSetDevice(previous);
+    }
+};
+
+size_t elem_size(int dtype) { return dtype == kF64 ? 8 : dtype == kF32 ? 4 : 2; }
+size_t acc_size(int dtype) { return dtype == kF64 ? 8 : 4; }
+
+struct DeviceInfo {
+    size_t smem_optin = 0;
+    int sm_count = 0;
+};
+DeviceInfo device_info(int device) {
+    static std::mutex mutex;
+    static std::map<int, DeviceInfo> cache;
+    const std::scoped_lock lock(mutex);
+    auto it = cache.find(device);
+    if (it != cache.end()) return it->second;
+    DeviceInfo info;
+    int v = 0;
+    SB_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, device));
+    info.smem_optin = static_cast<size_t>(v);
+    SB_CUDA(cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, device));
+    info.sm_count = v;
+    cache[device] = info;
+    return info;
+}
+
+// ------------------------------------------------------------------------------------------------
+// geometry and validation
+// ------------------------------------------------------------------------------------------------
+struct Geometry {
+    int64_t N = 0, C = 0, H = 0, W = 0;
+    int64_t kH = 0, kW = 0, kcs = 0;
+    int64_t numel() const { return N * C * H * W; }
+    int64_t kernel_numel() const { return kcs ? C * kcs : kH * kW; }
+};
+
+Geometry parse_geometry(const char* name, const int64_t* in_sizes, int64_t in_dim, const int64_t* k_sizes,
+                        int64_t k_dim) {
+    SB_CHECK(in_dim == 4, name, ": input must be 4-D (N, C, H, W), got ", in_dim, "-D");
+    SB_CHECK(k_dim == 2 || k_dim == 3, name, ": kernel must be 2-D (kH, kW) or 3-D (C, kH, kW), got ", k_dim, "-D");
+    SB_CHECK(in_sizes != nullptr && k_sizes != nullptr, name, ": sizes must not be null");
+    Geometry g;
+    g.N = in_sizes[0];
+    g.C = in_sizes[1];
+    g.H = in_sizes[2];
+    g.W = in_sizes[3];
+    SB_CHECK(g.N >= 0 && g.C >= 0 && g.H >= 0 && g.W >= 0, name, ": input sizes must be non-negative");
+    if (k_dim == 3) {
+        SB_CHECK(k_sizes[0] == g.C, name, ": kernel channel dim (", k_sizes[0], ") must match input channels (", g.C,
+                 ")");
+        g.kH = k_sizes[1];
+        g.kW = k_sizes[2];
+        g.kcs = g.kH * g.kW;
+    } else {
+        g.kH = k_sizes[0];
+        g.kW = k_sizes[1];
+        g.kcs = 0;
+    }
+    SB_CHECK(g.kH > 0 && g.kW > 0, name, ": kernel spatial dims must be positive");
+    SB_CHECK(g.H < (int64_t(1) << 30) && g.W < (int64_t(1) << 30) && g.kH < (int64_t(1) << 20) &&
+                 g.kW < (int64_t(1) << 20) && g.C < (int64_t(1) << 31),
+             name, ": extents beyond the supported range (H, W < 2^30, kH, kW < 2^20)");
+    return g;
+}
+
+void check_common(const char* name, int32_t dtype, int64_t border) {
+    SB_CHECK(dtype >= kF32 && dtype <= kBF16, name, ": unsupported dtype code ", dtype);
+    SB_CHECK(border >= kReflect && border <= kConstant, name, ": invalid border mode ", border);
+}
+
+int parse_algo(const char* name, int64_t algo) {
+    SB_CHECK(algo >= 0 && algo <= 3, name, ": invalid algo ", algo);
+    return static_cast<int>(algo);
+}
+
+// Flatness of the SE, read back from the device when the caller does not know it (a synchronising
+// copy on `stream`, as the reference does).
+bool resolve_flat(int32_t flat, const void* kernel, int64_t numel, int32_t dtype, cudaStream_t stream) {
+    if (flat >= 0) return flat != 0;
+    if (numel == 0) return true;
+    std::vector<unsigned char> host(static_cast<size_t>(numel) * elem_size(dtype));
+    SB_CUDA(cudaMemcpyAsync(host.data(), kernel, host.size(), cudaMemcpyDeviceToHost, stream));
+    SB_CUDA(cudaStreamSynchronize(stream));
+    for (int64_t i = 0; i < numel; ++i) {
+        float v = 0.0f;
+        switch (dtype) {
+        case kF32: std::memcpy(&v, host.data() + 4 * i, 4); break;
+        case kF64: {
+            double d;
+            std::memcpy(&d, host.data() + 8 * i, 8);
+            if (d != 0.0) return false;
+            continue;
+        }
+        default: {
+            uint16_t h;
+            std::memcpy(&h, host.data() + 2 * i, 2);
+            // zero in both half and bfloat16: only +0 and -0
+            if ((h & 0x7fffu) != 0) return false;
+            continue;
+        }
+        }
+        if (v != 0.0f) return false;
+    }
+    return true;
+}
+
+// ------------------------------------------------------------------------------------------------
+// thresholds (csrc/gpu/morphology/thresholds.h:46-71)
+// ------------------------------------------------------------------------------------------------
+constexpr int64_t kDefaultSeparableMinK = 11;
+
+int64_t separable_min_k_override() {
+    static const int64_t value = [] {
+        if (const char* env = std::getenv("SERRON_SEPARABLE_MIN_K")) {
+            char* end = nullptr;
+            const long parsed = std::strtol(env, &end, 10);
+            if (end != env && *end == '\0' && parsed > 0) return static_cast<int64_t>(parsed);
+        }
+        return static_cast<int64_t>(0);
+    }();
+    return value;
+}
+
+struct ThresholdTable {
+    std::mutex mutex;
+    std::map<std::tuple<int, int, bool>, int64_t> values;
+};
+ThresholdTable& thresholds() {
+    static ThresholdTable table;
+    return table;
+}
+
+int64_t separable_min_k(int device, int dtype, bool backward) {
+    if (const int64_t forced = separable_min_k_override(); forced > 0) return forced;
+    auto& t = thresholds();
+    const std::scoped_lock lock(t.mutex);
+    const auto it = t.values.find({device, dtype, backward});
+    return it == t.values.end() ? kDefaultSeparableMinK : it->second;
+}
+
+// ------------------------------------------------------------------------------------------------
+// algorithm feasibility and resolution (csrc/gpu/morphology/algorithm.h:59-137)
+// ------------------------------------------------------------------------------------------------
+enum Algo : int { kAuto = 0, kElement = 1, kTiled = 2, kSeparable = 3 };
+
+int direct_format(int64_t kH, int64_t kW) {
+    const int64_t taps = kH * kW;
+    return taps <= 255 ? SERRON_WINNERS_DIRECT_U8 : taps <= 65535 ? SERRON_WINNERS_DIRECT_U16 : SERRON_WINNERS_DIRECT_U32;
+}
+int separable_format(int64_t kH, int64_t kW) {
+    if (kH <= 15 && kW <= 16) return SERRON_WINNERS_SEPARABLE_U8;
+    if (kH <= 255 && kW <= 256) return SERRON_WINNERS_SEPARABLE_U16;
+    return SERRON_WINNERS_SEPARABLE_U32;
+}
+int format_bytes(int fmt) {
+    switch (fmt) {
+    case SERRON_WINNERS_DIRECT_U8:
+    case SERRON_WINNERS_SEPARABLE_U8: return 1;
+    case SERRON_WINNERS_DIRECT_U16:
+    case SERRON_WINNERS_SEPARABLE_U16: return 2;
+    case SERRON_WINNERS_DIRECT_U32:
+    case SERRON_WINNERS_SEPARABLE_U32: return 4;
+    default: return 0;
+    }
+}
+bool format_is_separable(int fmt) { return fmt >= SERRON_WINNERS_SEPARABLE_U8; }
+
+size_t tiled_smem_bytes(int64_t kH, int64_t kW, int dtype) {
+    return static_cast<size_t>((kTile + kH - 1) * (kTile + kW - 1) + kH * kW) * acc_size(dtype);
+}
+size_t gather_smem_bytes(int64_t kH, int64_t kW, int dtype, int fmt, bool sep) {
+    const int64_t tw = sep ? kGTW : kTile, th = sep ? kGTH : kTile;
+    return static_cast<size_t>((tw + kW - 1) * (th + kH - 1)) * (acc_size(dtype) + format_bytes(fmt)) + 16;
+}
+size_t sep_smem_bytes(int64_t kH, int64_t kW, int dtype) {
+    return dtype == kF64 ? SepSmem<double>::bytes(static_cast<int>(kH), static_cast<int>(kW))
+                         : SepSmem<float>::bytes(static_cast<int>(kH), static_cast<int>(kW));
+}
+
+struct Problem {
+    int64_t kH, kW;
+    bool flat;
+    int dtype;
+    size_t budget;
+    int64_t min_k;
+};
+
+bool tiled_feasible(const Problem& p) { return tiled_smem_bytes(p.kH, p.kW, p.dtype) <= p.budget; }
+bool separable_feasible(const Problem& p) {
+    return p.flat && p.kW <= 256 && p.kH <= 65534 && p.kH + kSepTH < 65536 && p.kW + kSepTW < 65536 &&
+           sep_smem_bytes(p.kH, p.kW, p.dtype) <= p.budget;
+}
+int heuristic(const Problem& p) {
+    if (std::max(p.kH, p.kW) >= p.min_k && separable_feasible(p)) return kSeparable;
+    return tiled_feasible(p) ? kTiled : kElement;
+}
+int resolve_algorithm(int requested, const Problem& p, const char* name) {
+    switch (requested) {
+    case kAuto: return heuristic(p);
+    case kElement: return kElement;
+    case kTiled:
+        SB_CHECK(tiled_feasible(p), name, ": algo 'tiled' needs ", tiled_smem_bytes(p.kH, p.kW, p.dtype),
+                 " bytes of shared memory for a ", p.kH, "x", p.kW, " window, over the ", p.budget, " available");
+        return kTiled;
+    default:
+        SB_CHECK(p.flat, name, ": algo 'separable' needs a flat structuring element");
+        SB_CHECK(separable_feasible(p), name, ": algo 'separable' does not fit in shared memory for a ", p.kH, "x",
+                 p.kW, " window");
+        return kSeparable;
+    }
+}
+int winners_format_for(int algo, int64_t kH, int64_t kW) {
+    return algo == kSeparable ? separable_format(kH, kW) : direct_format(kH, kW);
+}
+
+// ------------------------------------------------------------------------------------------------
+// type dispatch
+// ------------------------------------------------------------------------------------------------
+template <typename F>
+void dispatch_dtype(int dtype, F&& f) {
+    switch (dtype) {
+    case kF32: f(float{}); break;
+    case kF64: f(double{}); break;
+    case kF16: f(__half{}); break;
+    default: f(__nv_bfloat16{}); break;
+    }
+}
+template <typename F>
+void dispatch_op(int op, F&& f) {
+    if (op == kErode)
+        f(std::integral_constant<int, kErode>{});
+    else
+        f(std::integral_constant<int, kDilate>{});
+}
+template <typename F>
+void dispatch_index(int fmt, F&& f) {
+    switch (format_bytes(fmt)) {
+    case 1: f(uint8_t{}); break;
+    case 2: f(uint16_t{}); break;
+    default: f(uint32_t{}); break;
+    }
+}
+
+template <typename K>
+void set_smem(K kernel, size_t bytes) {
+    if (bytes > 48 * 1024) SB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
+}
+
+unsigned int grid_1d(long long blocks) {
+    SB_CHECK(blocks < (1ll << 31), "serron: problem too large for one launch");
+    return static_cast<unsigned int>(blocks);
+}
+
+// ------------------------------------------------------------------------------------------------
+// launches
+// ------------------------------------------------------------------------------------------------
+template <typename T, int OP, typename I, bool V, bool X>
+void launch_forward_t(int algo, const Geometry& g, const void* x, const void* w, void* y, void* win, int border,
+                      cudaStream_t stream) {
+    const int H = static_cast<int>(g.H), W = static_cast<int>(g.W), C = static_cast<int>(g.C);
+    const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW), kcs = static_cast<int>(g.kcs);
+    const T* xp = static_cast<const T*>(x);
+    const T* wp = static_cast<const T*>(w);
+    T* yp = static_cast<T*>(y);
+    I* ip = static_cast<I*>(win);
+    if (algo == kElement) {
+        const long long total = g.numel();
+        element_fwd_kernel<T, OP, I, V, X><<<grid_1d((total + 255) / 256), 256, 0, stream>>>(
+            xp, wp, yp, ip, total, C, H, W, kH, kW, kcs, border);
+    } else if (algo == kTiled) {
+        const int tx = ceil_div(W, kTile), ty = ceil_div(H, kTile);
+        const size_t smem = tiled_smem_bytes(kH, kW, std::is_same<T, double>::value ? kF64 : kF32);
+        auto kernel = tiled_fwd_kernel<T, OP, I, V, X>;
+        set_smem(kernel, smem);
+        kernel<<<grid_1d(static_cast<long long>(tx) * ty * g.N * g.C), dim3(kTile, kTileThreadsY), smem, stream>>>(
+            xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty);
+    } else {
+        const int tx = ceil_div(W, kSepTW), ty = ceil_div(H, kSepTH);
+        const size_t smem = SepSmem<typename Storage<T>::acc>::bytes(kH, kW);
+        auto kernel = sep_fwd_kernel<T, OP, I, V, X>;
+        set_smem(kernel, smem);
+        kernel<<<grid_1d(static_cast<long long>(tx) * ty * g.N * g.C), kSepThreads, smem, stream>>>(
+            xp, yp, ip, H, W, kH, kW, border, tx, ty);
+    }
+    SB_CUDA(cudaGetLastError());
+}
+
+void launch_forward(int op, int dtype, int algo, const Geometry& g, const void* x, const void* w, void* y, void* win,
+                    int fmt, int border, cudaStream_t stream) {
+    dispatch_dtype(dtype, [&](auto t) {
+        using T = decltype(t);
+        dispatch_op(op, [&](auto o) {
+            constexpr int OP = decltype(o)::value;
+            if (win == nullptr) {
+                launch_forward_t<T, OP, uint8_t, true, false>(algo, g, x, w, y, nullptr, border, stream);
+                return;
+            }
+            dispatch_index(fmt, [&](auto i) {
+                using I = decltype(i);
+                if (y != nullptr)
+                    launch_forward_t<T, OP, I, true, true>(algo, g, x, w, y, win, border, stream);
+                else
+                    launch_forward_t<T, OP, I, false, true>(algo, g, x, w, nullptr, win, border, stream);
+            });
+        });
+    });
+}
+
+// backward workspace layout: [winners][segrad partials][segrad global bins], each 256-byte aligned
+struct SegradPlan {
+    int chunks = 0;
+    int threads = 0;
+    bool global_bins = false;
+    long long per_chunk = 0;
+    int64_t partial_bytes = 0;
+    int64_t bins_bytes = 0;
+};
+SegradPlan segrad_plan(const Geometry& g) {
+    SegradPlan p;
+    const int64_t bins = g.kH * g.kW;
+    const int64_t per_channel = g.N * g.H * g.W;
+    const int64_t max_chunks = std::max<int64_t>(1, 592 / std::max<int64_t>(g.C, 1));
+    p.chunks = static_cast<int>(std::clamp<int64_t>((per_channel + 16383) / 16384, 1, max_chunks));
+    p.per_chunk = (per_channel + p.chunks - 1) / p.chunks;
+    if (bins <= 96) {
+        p.threads = 128;
+    } else if (bins <= 768) {
+        p.threads = 32;
+    } else {
+        p.threads = 32;
+        p.global_bins = true;
+    }
+    p.partial_bytes = g.C * p.chunks * bins * 8;
+    p.bins_bytes = p.global_bins ? g.C * p.chunks * int64_t(p.threads) * bins * 8 : 0;
+    return p;
+}
+int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+
+int64_t backward_workspace(const Geometry& g, bool need_kg, int fmt, bool with_winners) {
+    int64_t bytes = 0;
+    if (!with_winners) bytes += align256(g.numel() * format_bytes(fmt));
+    if (need_kg) {
+        const SegradPlan p = segrad_plan(g);
+        bytes += align256(p.partial_bytes) + align256(p.bins_bytes);
+    }
+    return bytes;
+}
+
+template <typename T, typename I, bool SEP>
+void launch_gather_t(const Geometry& g, const void* go, const void* win, void* gi, int border, size_t budget,
+                     cudaStream_t stream) {
+    const int H = static_cast<int>(g.H), W = static_cast<int>(g.W);
+    const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW);
+    const int dtype = std::is_same<T, double>::value ? kF64 : kF32;
+    const int fmt_bytes = sizeof(I);
+    const int tw = SEP ? kGTW : kTile, th = SEP ? kGTH : kTile;
+    const int tx = ceil_div(W, tw), ty = ceil_div(H, th);
+    size_t smem = static_cast<size_t>((tw + kW - 1) * (th + kH - 1)) * (acc_size(dtype) + fmt_bytes) + 16;
+    const long long blocks = static_cast<long long>(tx) * ty * g.N * g.C;
+    // a halo too large for shared memory walks the candidates in global memory instead
+    const int force_global = smem > budget ? 1 : 0;
+    if (force_global) smem = 0;
+    if (SEP) {
+        auto kernel = sep_gather_kernel<T, I>;
+        set_smem(kernel, smem);
+        kernel<<<grid_1d(blocks), dim3(kGTW, 8), smem, stream>>>(static_cast<const T*>(go), static_cast<const I*>(win),
+                                                               static_cast<T*>(gi), H, W, kH, kW, border, tx, ty,
+                                                               force_global);
+    } else {
+        auto kernel = direct_gather_kernel<T, I>;
+        set_smem(kernel, smem);
+        kernel<<<grid_1d(blocks), dim3(kTile, kTileThreadsY), smem, stream>>>(
+            static_cast<const T*>(go), static_cast<const I*>(win), static_cast<T*>(gi), static_cast<int>(g.C), H, W,
+            kH, kW, border, tx, ty, force_global);
+    }
+    SB_CUDA(cudaGetLastError());
+}
+
+template <typename T, typename I, bool SEP>
+void launch_segrad_t(int op, const Geometry& g, const void* go, const void* win, void* gk, void* ws, int border,
+                     cudaStream_t stream) {
+    const SegradPlan p = segrad_plan(g);
+    const int bins = static_cast<int>(g.kH * g.kW);
+    double* partial = static_cast<double*>(ws);
+    double* gbins = p.global_bins ? reinterpret_cast<double*>(static_cast<char*>(ws) + align256(p.partial_bytes)) : nullptr;
+    const size_t smem = p.global_bins ? 0 : static_cast<size_t>(p.threads) * bins * 8;
+    auto kernel = segrad_partial_kernel<T, I, SEP>;
+    set_smem(kernel, smem);
+    kernel<<<dim3(p.chunks, static_cast<unsigned>(g.C)), p.threads, smem, stream>>>(
+        static_cast<const T*>(go), static_cast<const I*>(win), partial, gbins, static_cast<int>(g.N),
+        static_cast<int>(g.C), static_cast<int>(g.H), static_cast<int>(g.W), static_cast<int>(g.kH),
+        static_cast<int>(g.kW), border, p.per_chunk);
+    SB_CUDA(cudaGetLastError());
+    const int out_cells = static_cast<int>(g.kcs ? g.C * bins : bins);
+    const double sign = op == kErode ? -1.0 : 1.0;
+    segrad_final_kernel<T><<<ceil_div(out_cells, 128), 128, 0, stream>>>(partial, static_cast<T*>(gk),
+                                                                          static_cast<int>(g.C), p.chunks, bins,
+                                                                          g.kcs ? 0 : 1, sign);
+    SB_CUDA(cudaGetLastError());
+}
+
+void launch_backward_from_winners(int op, int dtype, const Geometry& g, const void* go, const void* win, int fmt,
+                                  void* gi, void* gk, bool need_kg, void* ws, int border, size_t budget,
+                                  cudaStream_t stream) {
+    const bool sep = format_is_separable(fmt);
+    dispatch_dtype(dtype, [&](auto t) {
+        using T = decltype(t);
+        dispatch_index(fmt, [&](auto i) {
+            using I = decltype(i);
+            if (sep)
+                launch_gather_t<T, I, true>(g, go, win, gi, border, budget, stream);
+            else
+                launch_gather_t<T, I, false>(g, go, win, gi, border, budget, stream);
+            if (need_kg) {
+                if (sep)
+                    launch_segrad_t<T, I, true>(op, g, go, win, gk, ws, border, stream);
+                else
+                    launch_segrad_t<T, I, false>(op, g, go, win, gk, ws, border, stream);
+            }
+        });
+    });
+    if (!need_kg) SB_CUDA(cudaMemsetAsync(gk, 0, g.kernel_numel() * elem_size(dtype), stream));
+}
+
+const char* op_name(int op) { return op == kErode ? "serron::erode" : "serron::dilate"; }
+const char* bwd_name(int op) { return op == kErode ? "serron::erode_backward" : "serron::dilate_backward"; }
+
+int forward_impl(int op, const void* input, const int64_t* in_sizes, int64_t in_dim, const void* kernel,
+                 const int64_t* k_sizes, int64_t k_dim, int32_t dtype, int64_t border, int32_t flat, int64_t algo,
+                 void* output, void* winners, int32_t winners_format, int32_t device, void* stream_) {
+    return guarded([&] {
+        const char* name = op_name(op);
+        SB_CHECK(op == kErode || op == kDilate, "serron: invalid op ", op);
+        const Geometry g = parse_geometry(name, in_sizes, in_dim, k_sizes, k_dim);
+        check_common(name, dtype, border);
+        const int requested = parse_algo(name, algo);
+        if (g.numel() == 0) return;
+        SB_CHECK(input && kernel && (output || winners), name, ": null tensor pointer");
+        DeviceScope scope(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+        const DeviceInfo info = device_info(device);
+        // a forced tiled or element-wise launch never reads the flatness
+        const bool needs_flat = requested == kAuto || requested == kSeparable;
+        const bool is_flat = needs_flat && resolve_flat(flat, kernel, g.kernel_numel(), dtype, stream);
+        const Problem p{g.kH, g.kW, is_flat, dtype, info.smem_optin, separable_min_k(device, dtype, false)};
+        const int resolved = resolve_algorithm(requested, p, name);
+        if (winners) {
+            const int want = winners_format_for(resolved, g.kH, g.kW);
+            SB_CHECK(winners_format == want, name, ": winner format ", winners_format,
+                     " does not match the resolved algorithm (expected ", want, ")");
+        }
+        launch_forward(op, dtype, resolved, g, input, kernel, output, winners, winners_format, static_cast<int>(border),
+                       stream);
+    });
+}
+
+int backward_impl(int op, const void* grad_output, const int64_t* go_sizes, int64_t go_dim, const void* input,
+                  const int64_t* in_sizes, int64_t in_dim, const void* kernel, const int64_t* k_sizes, int64_t k_dim,
+                  int32_t dtype, int64_t border, int32_t flat, int32_t need_kg, int64_t algo, void* grad_input,
+                  void* grad_kernel, void* workspace, int64_t workspace_bytes, int32_t device, void* stream_) {
+    return guarded([&] {
+        const char* name = bwd_name(op);
+        const Geometry g = parse_geometry(name, in_sizes, in_dim, k_sizes, k_dim);
+        SB_CHECK(go_dim == 4, name, ": grad_output must be 4-D (N, C, H, W), got ", go_dim, "-D");
+        check_common(name, dtype, border);
+        const int requested = parse_algo(name, algo);
+        SB_CHECK(go_sizes[0] == g.N && go_sizes[1] == g.C && go_sizes[2] == g.H && go_sizes[3] == g.W, name,
+                 ": grad_output shape must match input");
+        DeviceScope scope(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+        if (g.numel() == 0) {
+            if (g.kernel_numel() > 0) SB_CUDA(cudaMemsetAsync(grad_kernel, 0, g.kernel_numel() * elem_size(dtype), stream));
+            return;
+        }
+        SB_CHECK(grad_output && input && kernel && grad_input && grad_kernel, name, ": null tensor pointer");
+        const DeviceInfo info = device_info(device);
+        const bool needs_flat = requested == kAuto || requested == kSeparable;
+        const bool is_flat = needs_flat && resolve_flat(flat, kernel, g.kernel_numel(), dtype, stream);
+        const Problem p{g.kH, g.kW, is_flat, dtype, info.smem_optin, separable_min_k(device, dtype, true)};
+        const int resolved = resolve_algorithm(requested, p, name);
+        const int fmt = winners_format_for(resolved, g.kH, g.kW);
+        const int64_t need = backward_workspace(g, need_kg != 0, fmt, false);
+        if (workspace_bytes < need)
+            throw Failure{SERRON_ERR_WORKSPACE, concat(name, ": workspace of ", workspace_bytes, " bytes, ", need, " needed")};
+        char* ws = static_cast<char*>(workspace);
+        void* win = ws;
+        launch_forward(op, dtype, resolved, g, input, kernel, nullptr, win, fmt, static_cast<int>(border), stream);
+        launch_backward_from_winners(op, dtype, g, grad_output, win, fmt, grad_input, grad_kernel, need_kg != 0,
+                                     ws + align256(g.numel() * format_bytes(fmt)), static_cast<int>(border),
+                                     info.smem_optin, stream);
+    });
+}
+
+// ------------------------------------------------------------------------------------------------
+// reconstruction
+// ------------------------------------------------------------------------------------------------
+int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const int64_t* sizes, int64_t dim,
+                     const void* kernel, const int64_t* k_sizes, int64_t k_dim, int32_t dtype, int64_t border,
+                     int64_t max_iter, int64_t check_every, void* output, void* workspace, int64_t workspace_bytes,
+                     int32_t device, void* stream_, int64_t* steps) {
+    return guarded([&] {
+        const char* name = dilate ? "serron.reconstruction_by_dilation" : "serron.reconstruction_by_erosion";
+        const Geometry g = parse_geometry(name, sizes, dim, k_sizes, k_dim);
+        check_common(name, dtype, border);
+        SB_CHECK(check_every >= 1, name, ": check_every must be >= 1, got ", check_every);
+        const int64_t total = g.numel();
+        const int64_t need = serron_reconstruct_workspace_bytes(sizes, dim, dtype, max_iter);
+        if (workspace_bytes < need)
+            throw Failure{SERRON_ERR_WORKSPACE, concat(name, ": workspace of ", workspace_bytes, " bytes, ", need, " needed")};
+        if (steps) *steps = 0;
+        if (total == 0) return;
+        DeviceScope scope(device);
+        cudaStream_t stream = static_cast<cudaStream_t>(stream_);
+        int* flags = static_cast<int*>(workspace);
+        void* tmp = static_cast<char*>(workspace) + 256;
+        const int H = static_cast<int>(g.H), W = static_cast<int>(g.W), C = static_cast<int>(g.C);
+        const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW), kcs = static_cast<int>(g.kcs);
+        const int op = dilate ? kDilate : kErode;
+        int host_flags[2] = {0, 0};
+        int64_t taken = 0;
+        bool converged = false;
+        dispatch_dtype(dtype, [&](auto t) {
+            using T = decltype(t);
+            dispatch_op(op, [&](auto o) {
+                constexpr int OP = decltype(o)::value;
+                SB_CUDA(cudaMemsetAsync(flags, 0, 2 * sizeof(int), stream));
+                recon_init_kernel<T, OP><<<grid_1d((total + 255) / 256), 256, 0, stream>>>(
+                    static_cast<const T*>(marker), static_cast<const T*>(mask), static_cast<T*>(output), total, flags);
+                SB_CUDA(cudaGetLastError());
+                SB_CUDA(cudaMemcpyAsync(host_flags, flags, 2 * sizeof(int), cudaMemcpyDeviceToHost, stream));
+                SB_CUDA(cudaStreamSynchronize(stream));
+                const bool has_nan = host_flags[1] != 0;
+                if (max_iter <= 0) {
+                    // a NaN never compares equal, so the reference's loop would never end
+                    if (has_nan)
+                        throw Failure{SERRON_ERR_NOT_CONVERGED,
+                                      concat(name, ": no fixed point after None iterations; raise max_iter, or pass "
+                                                   "finite inputs (a NaN never compares equal, so the convergence test "
+                                                   "can never fire)")};
+                    const int tx = ceil_div(W, kRecTile), ty = ceil_div(H, kRecTile);
+                    const size_t smem = (static_cast<size_t>(kRecTile + kW - 1) * (kRecTile + kH - 1) +
+                                         kRecTile * kRecTile + static_cast<size_t>(kH) * kW) *
+                                        sizeof(typename Storage<T>::acc);
+                    auto kernel_fn = recon_tile_kernel<T, OP>;
+                    set_smem(kernel_fn, smem);
+                    const long long blocks = static_cast<long long>(tx) * ty * g.N * g.C;
+                    const int64_t cap = 4 * (static_cast<int64_t>(H) * W + 16);
+                    for (;;) {
+                        SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
+                        kernel_fn<<<grid_1d(blocks), kRecThreads, smem, stream>>>(
+                            static_cast<T*>(output), static_cast<const T*>(mask), static_cast<const T*>(kernel), C, H,
+                            W, kH, kW, kcs, static_cast<int>(border), tx, ty, 4 * kRecTile, flags);
+                        SB_CUDA(cudaGetLastError());
+                        ++taken;
+                        SB_CUDA(cudaMemcpyAsync(host_flags, flags, sizeof(int), cudaMemcpyDeviceToHost, stream));
+                        SB_CUDA(cudaStreamSynchronize(stream));
+                        if (host_flags[0] == 0) {
+                            converged = true;
+                            break;
+                        }
+                        SB_CHECK(taken < cap, name, ": relaxation did not settle");
+                    }
+                } else {
+                    // the reference's Jacobi schedule: check every `check_every` steps, stop at max_iter
+                    T* cur = static_cast<T*>(output);
+                    T* nxt = static_cast<T*>(tmp);
+                    for (int64_t it = 1; it <= max_iter; ++it) {
+                        recon_step_kernel<T, OP><<<grid_1d((total + 255) / 256), 256, 0, stream>>>(
+                            cur, nxt, static_cast<const T*>(mask), static_cast<const T*>(kernel), total, C, H, W, kH,
+                            kW, kcs, static_cast<int>(border), flags);
+                        SB_CUDA(cudaGetLastError());
+                        std::swap(cur, nxt);
+                        taken = it;
+                        if (it % check_every == 0) {
+                            SB_CUDA(cudaMemcpyAsync(host_flags, flags, sizeof(int), cudaMemcpyDeviceToHost, stream));
+                            SB_CUDA(cudaStreamSynchronize(stream));
+                            if (host_flags[0] == 0 && !has_nan) {
+                                converged = true;
+                                break;
+                            }
+                            SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
+                        }
+                    }
+                    if (!converged) {
+                        SB_CUDA(cudaMemcpyAsync(host_flags, flags, sizeof(int), cudaMemcpyDeviceToHost, stream));
+                        SB_CUDA(cudaStreamSynchronize(stream));
+                        converged = host_flags[0] == 0 && !has_nan;
+                    }
+                    if (cur != static_cast<T*>(output))
+                        SB_CUDA(cudaMemcpyAsync(output, cur, total * sizeof(T), cudaMemcpyDeviceToDevice, stream));
+                    if (!converged)
+                        throw Failure{SERRON_ERR_NOT_CONVERGED,
+                                      concat(name, ": no fixed point after ", max_iter,
+                                             " iterations; raise max_iter, or pass finite inputs (a NaN never "
+                                             "compares equal, so the convergence test can never fire)")};
+                }
+            });
+        });
+        if (steps) *steps = taken;
+        (void)converged;
+    });
+}
+
+}  // namespace
+}  // namespace serron
+
+using namespace serron;
+
+extern "C" {
+
+const char* serron_last_error(void) { return g_last_error.c_str(); }
+
+int32_t serron_abi_version(void) { return 1; }
+
+int serron_erode(const void* input, const int64_t* input_sizes, int64_t input_dim, const void* kernel,
+                 const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype, int64_t border, int32_t flat,
+                 int64_t algo, void* output, int32_t device, void* stream) {
+    return forward_impl(kErode, input, input_sizes, input_dim, kernel, kernel_sizes, kernel_dim, dtype, border, flat,
+                        algo, output, nullptr, 0, device, stream);
+}
+
+int serron_dilate(const void* input, const int64_t* input_sizes, int64_t input_dim, const void* kernel,
+                  const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype, int64_t border, int32_t flat,
+                  int64_t algo, void* output, int32_t device, void* stream) {
+    return forward_impl(kDilate, input, input_sizes, input_dim, kernel, kernel_sizes, kernel_dim, dtype, border, flat,
+                        algo, output, nullptr, 0, device, stream);
+}
+
+int serron_forward(int32_t op, const void* input, const int64_t* input_sizes, int64_t input_dim, const void* kernel,
+                   const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype, int64_t border, int32_t flat,
+                   int64_t algo, void* output, void* winners, int32_t winners_format, int32_t device, void* stream) {
+    return forward_impl(op, input, input_sizes, input_dim, kernel, kernel_sizes, kernel_dim, dtype, border, flat, algo,
+                        output, winners, winners_format, device, stream);
+}
+
+int serron_plan(const int64_t* input_sizes, int64_t input_dim, const void* kernel, const int64_t* kernel_sizes,
+                int64_t kernel_dim, int32_t dtype, int32_t flat, int64_t algo, int32_t backward, int32_t device,
+                void* stream, serron_plan_t* plan) {
+    return guarded([&] {
+        const char* name = backward ? "serron::plan(backward)" : "serron::plan";
+        const Geometry g = parse_geometry(name, input_sizes, input_dim, kernel_sizes, kernel_dim);
+        check_common(name, dtype, 0);
+        const int requested = parse_algo(name, algo);
+        SB_CHECK(plan != nullptr, name, ": plan must not be null");
+        DeviceScope scope(device);
+        const DeviceInfo info = device_info(device);
+        const bool needs_flat = requested == kAuto || requested == kSeparable;
+        const bool is_flat = needs_flat && resolve_flat(flat, kernel, g.kernel_numel(), dtype,
+                                                        static_cast<cudaStream_t>(stream));
+        const Problem p{g.kH, g.kW, is_flat, dtype, info.smem_optin, separable_min_k(device, dtype, backward != 0)};
+        const int resolved = resolve_algorithm(requested, p, name);
+        plan->algo = resolved;
+        plan->winners_format = winners_format_for(resolved, g.kH, g.kW);
+        plan->winners_bytes = format_bytes(plan->winners_format);
+        plan->reserved = 0;
+        plan->workspace_bytes = backward_workspace(g, true, plan->winners_format, false);
+    });
+}
+
+int serron_erode_backward(const void* grad_output, const int64_t* grad_output_sizes, int64_t grad_output_dim,
+                          const void* input, const int64_t* input_sizes, int64_t input_dim, const void* kernel,
+                          const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype, int64_t border, int32_t flat,
+                          int32_t need_kernel_grad, int64_t algo, void* grad_input, void* grad_kernel, void* workspace,
+                          int64_t workspace_bytes, int32_t device, void* stream) {
+    return backward_impl(kErode, grad_output, grad_output_sizes, grad_output_dim, input, input_sizes, input_dim, kernel,
+                         kernel_sizes, kernel_dim, dtype, border, flat, need_kernel_grad, algo, grad_input,
+                         grad_kernel, workspace, workspace_bytes, device, stream);
+}
+
+int serron_dilate_backward(const void* grad_output, const int64_t* grad_output_sizes, int64_t grad_output_dim,
+                           const void* input, const int64_t* input_sizes, int64_t input_dim, const void* kernel,
+                           const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype, int64_t border,
+                           int32_t flat, int32_t need_kernel_grad, int64_t algo, void* grad_input, void* grad_kernel,
+                           void* workspace, int64_t workspace_bytes, int32_t device, void* stream) {
+    return backward_impl(kDilate, grad_output, grad_output_sizes, grad_output_dim, input, input_sizes, input_dim,
+                         kernel, kernel_sizes, kernel_dim, dtype, border, flat, need_kernel_grad, algo, grad_input,
+                         grad_kernel, workspace, workspace_bytes, device, stream);
+}
+
+int serron_backward_from_winners(int32_t op, const void* grad_output, const int64_t* sizes, int64_t dim,
+                                 const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype, int64_t border,
+                                 int32_t need_kernel_grad, const void* winners, int32_t winners_format,
+                                 void* grad_input, void* grad_kernel, void* workspace, int64_t workspace_bytes,
+                                 int32_t device, void* stream) {
+    return guarded([&] {
+        const char* name = bwd_name(op);
+        SB_CHECK(op == kErode || op == kDilate, "serron: invalid op ", op);
+        const Geometry g = parse_geometry(name, sizes, dim, kernel_sizes, kernel_dim);
+        check_common(name, dtype, border);
+        SB_CHECK(winners_format >= SERRON_WINNERS_DIRECT_U8 && winners_format <= SERRON_WINNERS_SEPARABLE_U32, name,
+                 ": invalid winner format ", winners_format);
+        const int want = format_is_separable(winners_format) ? separable_format(g.kH, g.kW) : direct_format(g.kH, g.kW);
+        SB_CHECK(winners_format == want, name, ": winner format ", winners_format, " does not fit a ", g.kH, "x", g.kW,
+                 " window");
+        DeviceScope scope(device);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (g.numel() == 0) {
+            if (g.kernel_numel() > 0) SB_CUDA(cudaMemsetAsync(grad_kernel, 0, g.kernel_numel() * elem_size(dtype), s));
+            return;
+        }
+        const int64_t need = backward_workspace(g, need_kernel_grad != 0, winners_format, true);
+        if (workspace_bytes < need)
+            throw Failure{SERRON_ERR_WORKSPACE, concat(name, ": workspace of ", workspace_bytes, " bytes, ", need, " needed")};
+        SB_CHECK(grad_output && winners && grad_input && grad_kernel, name, ": null tensor pointer");
+        const DeviceInfo info = device_info(device);
+        launch_backward_from_winners(op, dtype, g, grad_output, winners, winners_format, grad_input, grad_kernel,
+                                     need_kernel_grad != 0, workspace, static_cast<int>(border), info.smem_optin, s);
+    });
+}
+
+int64_t serron_backward_workspace_bytes(const int64_t* sizes, int64_t dim, const int64_t* kernel_sizes,
+                                        int64_t kernel_dim, int32_t need_kernel_grad, int32_t winners_format,
+                                        int32_t with_winners) {
+    int64_t out = -1;
+    const int rc = guarded([&] {
+        const Geometry g = parse_geometry("serron::backward_workspace_bytes", sizes, dim, kernel_sizes, kernel_dim);
+        out = backward_workspace(g, need_kernel_grad != 0, winners_format, with_winners != 0);
+    });
+    return rc == SERRON_OK ? out : -1;
+}
+
+int64_t serron_feasible_algos(const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype, int32_t flat,
+                              int32_t backward, int32_t device) {
+    int64_t mask = -1;
+    const int rc = guarded([&] {
+        const char* name = "serron::feasible_algos";
+        SB_CHECK(kernel_dim == 2 || kernel_dim == 3, name, ": kernel must be 2-D (kH, kW) or 3-D (C, kH, kW), got ",
+                 kernel_dim, "-D");
+        const int64_t kH = kernel_sizes[kernel_dim - 2], kW = kernel_sizes[kernel_dim - 1];
+        SB_CHECK(kH > 0 && kW > 0, name, ": kernel spatial dims must be positive");
+        check_common(name, dtype, 0);
+        DeviceScope scope(device);
+        const Problem p{kH, kW, flat > 0, dtype, device_info(device).smem_optin,
+                        separable_min_k(device, dtype, backward != 0)};
+        mask = (int64_t(1) << kElement) | (tiled_feasible(p) ? (int64_t(1) << kTiled) : 0) |
+               (separable_feasible(p) ? (int64_t(1) << kSeparable) : 0);
+    });
+    return rc == SERRON_OK ? mask : -1;
+}
+
+int64_t serron_heuristic_algo(const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype, int32_t flat,
+                              int32_t backward, int32_t device) {
+    int64_t algo = -1;
+    const int rc = guarded([&] {
+        const char* name = "serron::heuristic_algo";
+        SB_CHECK(kernel_dim == 2 || kernel_dim == 3, name, ": kernel must be 2-D (kH, kW) or 3-D (C, kH, kW), got ",
+                 kernel_dim, "-D");
+        const int64_t kH = kernel_sizes[kernel_dim - 2], kW = kernel_sizes[kernel_dim - 1];
+        SB_CHECK(kH > 0 && kW > 0, name, ": kernel spatial dims must be positive");
+        check_common(name, dtype, 0);
+        DeviceScope scope(device);
+        const Problem p{kH, kW, flat > 0, dtype, device_info(device).smem_optin,
+                        separable_min_k(device, dtype, backward != 0)};
+        algo = heuristic(p);
+    });
+    return rc == SERRON_OK ? algo : -1;
+}
+
+int64_t serron_set_separable_min_k(int32_t device, int32_t dtype, int32_t backward, int64_t min_k) {
+    auto& t = thresholds();
+    {
+        const std::scoped_lock lock(t.mutex);
+        const std::tuple<int, int, bool> key{device, dtype, backward != 0};
+        if (min_k > 0)
+            t.values[key] = min_k;
+        else
+            t.values.erase(key);
+    }
+    return separable_min_k(device, dtype, backward != 0);
+}
+
+int64_t serron_get_separable_min_k(int32_t device, int32_t dtype, int32_t backward) {
+    return separable_min_k(device, dtype, backward != 0);
+}
+
+int serron_reconstruct(int32_t dilate, const void* marker, const void* mask, const int64_t* sizes, int64_t dim,
+                       const void* kernel, const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype,
+                       int64_t border, int64_t max_iter, int64_t check_every, void* output, void* workspace,
+                       int64_t workspace_bytes, int32_t device, void* stream, int64_t* steps) {
+    return reconstruct_impl(dilate, marker, mask, sizes, dim, kernel, kernel_sizes, kernel_dim, dtype, border, max_iter,
+                            check_every, output, workspace, workspace_bytes, device, stream, steps);
+}
+
+int64_t serron_reconstruct_workspace_bytes(const int64_t* sizes, int64_t dim, int32_t dtype, int64_t max_iter) {
+    if (dim != 4 || sizes == nullptr || dtype < kF32 || dtype > kBF16) return -1;
+    const int64_t total = sizes[0] * sizes[1] * sizes[2] * sizes[3];
+    return 256 + (max_iter > 0 ? align256(total * static_cast<int64_t>(elem_size(dtype))) : 0);
+}
+
+}  // extern "C"

@@ -1,0 +1,285 @@
+// Direct (2-D window) kernels: element-wise and shared-memory tiled forward, optionally recording
+// the winning tap, and the atomic-free gather that forms grad_input.
+//
+// Reference behaviour followed: forward csrc/gpu/morphology/forward_kernels.cu:43-178 and
+// csrc/cpu/morphology/operators.cpp:38-80; winner selection csrc/cpu/morphology/backward.cpp:46-99;
+// grad_input accumulation order and precision csrc/cpu/morphology/backward.cpp:250-263 (serial
+// scatter in output raster order, in the storage type's arithmetic).  The gather visits, for each
+// input pixel, the outputs that can select it in ascending raster order, so every sum is formed in
+// exactly the order and precision the reference CPU forms it, with no atomics.
+#pragma once
+
+#include "common.cuh"
+
+namespace serron {
+
+constexpr int kTile = 32;        // tiled forward / gather: 32x32 outputs (pixels) per CTA
+constexpr int kTileThreadsY = 8; // 32 x 8 threads, 4 rows per thread
+constexpr int kRowsPerThread = kTile / kTileThreadsY;
+
+// Decodes a 1-D grid index into (plane, tile row, tile column).
+struct TileCoord {
+    long long plane;
+    int ty, tx;
+};
+__device__ __forceinline__ TileCoord tile_coord(int tiles_x, int tiles_y) {
+    const long long b = blockIdx.x;
+    TileCoord t;
+    t.tx = static_cast<int>(b % tiles_x);
+    t.ty = static_cast<int>((b / tiles_x) % tiles_y);
+    t.plane = b / (static_cast<long long>(tiles_x) * tiles_y);
+    return t;
+}
+
+// ------------------------------------------------------------------------------------------------
+// winner search over one window
+//
+// `sample(di, dj, v)` stores the (border-resolved) sample and returns false when the tap lies outside
+// a CONSTANT border.  Returns the extreme value and the first strictly-improving tap, or tap = -1.
+// ------------------------------------------------------------------------------------------------
+template <typename T, int OP, bool EXACT, typename Sample, typename Weight>
+__device__ __forceinline__ void window_winner(const Sample& sample, const Weight& weight, int kH, int kW,
+                                              typename Storage<T>::acc& best_out, int& tap_out) {
+    using A = typename Storage<T>::acc;
+    const A neutral = Op<OP>::template neutral<A>();
+    A best = neutral;
+    int tap = -1;
+    bool tie = false;
+    for (int di = 0; di < kH; ++di) {
+        for (int dj = 0; dj < kW; ++dj) {
+            A s;
+            if (!sample(di, dj, s)) continue;  // CONSTANT outside: neutral, never wins
+            const A v = Op<OP>::tap(s, weight(di, dj));
+            if (EXACT) tie |= (v == best);
+            if (Op<OP>::better(v, best)) {
+                best = v;
+                tap = di * kW + dj;
+            }
+        }
+    }
+    if (EXACT && tie && best != neutral) {
+        // a float tie with the running best: settle it the way the reference CPU does, in double
+        double bd = Op<OP>::template neutral<double>();
+        tap = -1;
+        for (int di = 0; di < kH; ++di) {
+            for (int dj = 0; dj < kW; ++dj) {
+                A s;
+                if (!sample(di, dj, s)) continue;
+                const double v = Op<OP>::tap(static_cast<double>(s), static_cast<double>(weight(di, dj)));
+                if (Op<OP>::better(v, bd)) {
+                    bd = v;
+                    tap = di * kW + dj;
+                }
+            }
+        }
+    }
+    best_out = best;
+    tap_out = tap;
+}
+
+template <typename I>
+__device__ __forceinline__ I encode_direct(int tap) {
+    return tap < 0 ? static_cast<I>(IndexTraits<I>::none) : static_cast<I>(tap);
+}
+
+// ------------------------------------------------------------------------------------------------
+// element-wise forward (algo = element): one thread per output, samples read from global memory
+// ------------------------------------------------------------------------------------------------
+template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX>
+__global__ void __launch_bounds__(256) element_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                          T* __restrict__ y, I* __restrict__ win, long long total,
+                                                          int C, int H, int W, int kH, int kW, int kcs,
+                                                          int border) {
+    using A = typename Storage<T>::acc;
+    const long long idx = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
+    if (idx >= total) return;
+    const int ow = static_cast<int>(idx % W);
+    const int oh = static_cast<int>((idx / W) % H);
+    const long long plane = idx / (static_cast<long long>(W) * H);
+    const int c = static_cast<int>(plane % C);
+    const T* xp = x + plane * H * W;
+    const T* wc = w + static_cast<long long>(c) * kcs;
+    const int aH = kH / 2, aW = kW / 2;
+    auto sample = [&](int di, int dj, A& s) {
+        int r = oh + di - aH, q = ow + dj - aW;
+        if (!resolve(r, H, border) || !resolve(q, W, border)) return false;
+        s = Storage<T>::load(xp[static_cast<long long>(r) * W + q]);
+        return true;
+    };
+    auto weight = [&](int di, int dj) { return Storage<T>::load(wc[di * kW + dj]); };
+    A best;
+    int tap;
+    // float inputs always track ties here; a tied window is settled in double, which is exact for any
+    // weights (for 0/inf weights the redo merely repeats the float answer)
+    window_winner<T, OP, NeedsExactCheck<T>::value>(sample, weight, kH, kW, best, tap);
+    if (WITH_VALUE) y[idx] = Storage<T>::store(best);
+    if (WITH_INDEX) win[idx] = encode_direct<I>(tap);
+}
+
+// ------------------------------------------------------------------------------------------------
+// tiled forward (algo = tiled): a 32x32 output tile, its halo staged once in shared memory with the
+// border resolved at staging (CONSTANT cells hold the neutral element, which never wins)
+// ------------------------------------------------------------------------------------------------
+template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX>
+__global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                        T* __restrict__ y, I* __restrict__ win, int C, int H, int W,
+                                                        int kH, int kW, int kcs, int border, int tiles_x,
+                                                        int tiles_y) {
+    using A = typename Storage<T>::acc;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int sw = kTile + kW - 1, sh = kTile + kH - 1;
+    A* xs = reinterpret_cast<A*>(smem_raw);
+    A* ws = xs + sw * sh;
+    __shared__ int exact_flag;
+
+    const TileCoord tc = tile_coord(tiles_x, tiles_y);
+    const int c = static_cast<int>(tc.plane % C);
+    const int oh0 = tc.ty * kTile, ow0 = tc.tx * kTile;
+    const int aH = kH / 2, aW = kW / 2;
+    const T* xp = x + tc.plane * H * W;
+    const T* wc = w + static_cast<long long>(c) * kcs;
+    const int tid = threadIdx.y * kTile + threadIdx.x;
+    const A neutral = Op<OP>::template neutral<A>();
+
+    if (tid == 0) exact_flag = 1;
+    __syncthreads();
+    for (int i = tid; i < kH * kW; i += 256) {
+        const A v = Storage<T>::load(wc[i]);
+        ws[i] = v;
+        if (NeedsExactCheck<T>::value && !weight_is_exact(static_cast<float>(v))) exact_flag = 0;
+    }
+    for (int i = tid; i < sw * sh; i += 256) {
+        const int r = i / sw, q = i - r * sw;
+        int gr = oh0 - aH + r, gq = ow0 - aW + q;
+        A v = neutral;
+        if (resolve(gr, H, border) && resolve(gq, W, border)) v = Storage<T>::load(xp[static_cast<long long>(gr) * W + gq]);
+        xs[i] = v;
+    }
+    __syncthreads();
+
+    const int ow = ow0 + threadIdx.x;
+    const bool exact = !NeedsExactCheck<T>::value || exact_flag;
+#pragma unroll
+    for (int i = 0; i < kRowsPerThread; ++i) {
+        const int lr = threadIdx.y * kRowsPerThread + i;
+        const int oh = oh0 + lr;
+        if (oh >= H || ow >= W) continue;
+        auto sample = [&](int di, int dj, A& s) {
+            s = xs[(lr + di) * sw + threadIdx.x + dj];
+            return true;
+        };
+        auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
+        A best;
+        int tap;
+        if (exact)
+            window_winner<T, OP, false>(sample, weight, kH, kW, best, tap);
+        else
+            window_winner<T, OP, true>(sample, weight, kH, kW, best, tap);
+        const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
+        if (WITH_VALUE) y[o] = Storage<T>::store(best);
+        if (WITH_INDEX) win[o] = encode_direct<I>(tap);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
+// grad_input gather for direct winners
+//
+// Each CTA owns a 32x32 tile of input pixels and stages the winners and grad_output of every output
+// that can reach the tile.  A pixel walks its candidate outputs in ascending raster order and adds
+// grad_output wherever the output's winner resolves to it.
+// ------------------------------------------------------------------------------------------------
+template <typename T, typename I>
+__global__ void __launch_bounds__(256) direct_gather_kernel(const T* __restrict__ go, const I* __restrict__ win,
+                                                            T* __restrict__ gi, int C, int H, int W, int kH, int kW,
+                                                            int border, int tiles_x, int tiles_y, int force_global) {
+    using G = typename GradAcc<T>::type;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int aH = kH / 2, aW = kW / 2;
+    const int rh0 = -(kH - 1 - aH), rw0 = -(kW - 1 - aW);  // halo origin relative to the tile
+    const int sw = kTile + kW - 1, sh = kTile + kH - 1;
+    G* gs = reinterpret_cast<G*>(smem_raw);
+    I* is = reinterpret_cast<I*>(gs + sw * sh);
+
+    const TileCoord tc = tile_coord(tiles_x, tiles_y);
+    const int ph0 = tc.ty * kTile, pw0 = tc.tx * kTile;
+    const long long base = tc.plane * H * W;
+    const int tid = threadIdx.y * kTile + threadIdx.x;
+    const bool full_h = border == kReflect && (aH > H - 1 || kH - 1 - aH > H - 1);
+    const bool full_w = border == kReflect && (aW > W - 1 || kW - 1 - aW > W - 1);
+
+    if (force_global || full_h || full_w) {
+        // windows wider than the image under REFLECT (any output may fold back onto any pixel), or a
+        // halo too large for shared memory: walk the candidates in global memory
+        for (int i = 0; i < kRowsPerThread; ++i) {
+            const int ph = ph0 + threadIdx.y * kRowsPerThread + i, pw = pw0 + threadIdx.x;
+            if (ph >= H || pw >= W) continue;
+            int lh, hh, lw, hw;
+            candidate_range(ph, H, kH, aH, border, lh, hh);
+            candidate_range(pw, W, kW, aW, border, lw, hw);
+            G acc = G(0);
+            for (int oh = lh; oh <= hh; ++oh)
+                for (int ow = lw; ow <= hw; ++ow) {
+                    const long long o = base + static_cast<long long>(oh) * W + ow;
+                    const uint32_t t = win[o];
+                    if (t == IndexTraits<I>::none) continue;
+                    int r = oh + static_cast<int>(t / kW) - aH, q = ow + static_cast<int>(t % kW) - aW;
+                    if (resolve(r, H, border) && resolve(q, W, border) && r == ph && q == pw)
+                        acc = GradAcc<T>::add(acc, static_cast<G>(Storage<T>::load(go[o])));
+                }
+            gi[base + static_cast<long long>(ph) * W + pw] = Storage<T>::store(static_cast<typename Storage<T>::acc>(acc));
+        }
+        return;
+    }
+
+    for (int i = tid; i < sw * sh; i += 256) {
+        const int r = i / sw, q = i - r * sw;
+        const int oh = ph0 + rh0 + r, ow = pw0 + rw0 + q;
+        I t = static_cast<I>(IndexTraits<I>::none);
+        G g = G(0);
+        if (oh >= 0 && oh < H && ow >= 0 && ow < W) {
+            const long long o = base + static_cast<long long>(oh) * W + ow;
+            t = win[o];
+            g = static_cast<G>(Storage<T>::load(go[o]));
+        }
+        is[i] = t;
+        gs[i] = g;
+    }
+    __syncthreads();
+
+    const bool deep = ph0 >= kH - 1 && ph0 + kTile - 1 <= H - kH && pw0 >= kW - 1 && pw0 + kTile - 1 <= W - kW;
+    for (int i = 0; i < kRowsPerThread; ++i) {
+        const int lr = threadIdx.y * kRowsPerThread + i;
+        const int ph = ph0 + lr, pw = pw0 + threadIdx.x;
+        if (ph >= H || pw >= W) continue;
+        G acc = G(0);
+        if (deep) {
+            // no border mapping anywhere in reach: output (ph - aH' + a, ...) selects the pixel only
+            // through the tap that points straight at it
+            for (int a = 0; a < kH; ++a) {        // output row = ph + rh0 + a, ascending
+                const int di = kH - 1 - a;          // tap row pointing from that output to ph
+                const int srow = (lr + a) * sw + threadIdx.x;
+                for (int b = 0; b < kW; ++b) {
+                    const uint32_t want = static_cast<uint32_t>(di * kW + (kW - 1 - b));
+                    if (static_cast<uint32_t>(is[srow + b]) == want) acc = GradAcc<T>::add(acc, gs[srow + b]);
+                }
+            }
+        } else {
+            int lh, hh, lw, hw;
+            candidate_range(ph, H, kH, aH, border, lh, hh);
+            candidate_range(pw, W, kW, aW, border, lw, hw);
+            for (int oh = lh; oh <= hh; ++oh) {
+                const int srow = (oh - ph0 - rh0) * sw - pw0 - rw0;
+                for (int ow = lw; ow <= hw; ++ow) {
+                    const uint32_t t = is[srow + ow];
+                    if (t == IndexTraits<I>::none) continue;
+                    int r = oh + static_cast<int>(t / kW) - aH, q = ow + static_cast<int>(t % kW) - aW;
+                    if (resolve(r, H, border) && resolve(q, W, border) && r == ph && q == pw)
+                        acc = GradAcc<T>::add(acc, gs[srow + ow]);
+                }
+            }
+        }
+        gi[base + static_cast<long long>(ph) * W + pw] = Storage<T>::store(static_cast<typename Storage<T>::acc>(acc));
+    }
+}
+
+}  // namespace serron
