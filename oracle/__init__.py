@@ -119,6 +119,26 @@ def backward(op: int, go: torch.Tensor, x: torch.Tensor, w: torch.Tensor, border
     return gi, gk
 
 
+def grad_kernel_wide(op: int, go: torch.Tensor, x: torch.Tensor, w: torch.Tensor, border: int, *,
+                     separable: bool = False) -> torch.Tensor:
+    """grad_kernel summed in float64 and rounded once to the storage type.
+
+    The reference's CPU backward rounds half/bfloat16 sums to the storage type after every add
+    (csrc/cpu/morphology/backward.cpp:250-263), so its grad_kernel drifts with the number of terms;
+    its CUDA backward accumulates in float and rounds once (csrc/gpu/morphology/backward.cpp:196-203).
+    This is that single-rounding semantics, on the oracle's (bit-exact) winners.
+    """
+    go_c, x_c, w_c = _prep(go, x, w)
+    _, bk = winners(op, x_c, w_c, border, separable=separable)
+    sign = -1.0 if op == ERODE else 1.0
+    flat_go = go_c.reshape(-1).double()
+    flat_bk = bk.reshape(-1)
+    keep = flat_bk >= 0
+    acc = torch.zeros(w_c.numel(), dtype=torch.float64)
+    acc.index_add_(0, flat_bk[keep], flat_go[keep])
+    return (sign * acc).reshape(w_c.shape).to(w_c.dtype)
+
+
 def reconstruct(dilate: bool, marker: torch.Tensor, mask: torch.Tensor, w: torch.Tensor, border: int, *,
                 max_iter: int | None = None, check_every: int = 16) -> tuple[torch.Tensor, int]:
     """Geodesic reconstruction; returns (result, steps).  Raises when max_iter runs out."""

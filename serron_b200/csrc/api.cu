@@ -252,7 +252,7 @@ size_t tiled_smem_bytes(int64_t kH, int64_t kW, int dtype) {
 }
 size_t gather_smem_bytes(int64_t kH, int64_t kW, int dtype, int fmt, bool sep) {
     const int64_t tw = sep ? kGTW : kTile, th = sep ? kGTH : kTile;
-    return static_cast<size_t>((tw + kW - 1) * (th + kH - 1)) * (acc_size(dtype) + format_bytes(fmt)) + 16;
+    return static_cast<size_t>((tw + 2 * (kW / 2)) * (th + 2 * (kH / 2))) * (acc_size(dtype) + format_bytes(fmt)) + 16;
 }
 size_t sep_smem_bytes(int64_t kH, int64_t kW, int dtype) {
     return dtype == kF64 ? SepSmem<double>::bytes(static_cast<int>(kH), static_cast<int>(kW))
@@ -437,7 +437,7 @@ void launch_gather_t(const Geometry& g, const void* go, const void* win, void* g
     const int fmt_bytes = sizeof(I);
     const int tw = SEP ? kGTW : kTile, th = SEP ? kGTH : kTile;
     const int tx = ceil_div(W, tw), ty = ceil_div(H, th);
-    size_t smem = static_cast<size_t>((tw + kW - 1) * (th + kH - 1)) * (acc_size(dtype) + fmt_bytes) + 16;
+    size_t smem = static_cast<size_t>((tw + 2 * (kW / 2)) * (th + 2 * (kH / 2))) * (acc_size(dtype) + fmt_bytes) + 16;
     const long long blocks = static_cast<long long>(tx) * ty * g.N * g.C;
     // a halo too large for shared memory walks the candidates in global memory instead
     const int force_global = smem > budget ? 1 : 0;

@@ -110,9 +110,12 @@ __device__ __forceinline__ bool resolve(int& c, int size, int border) {
     return false;
 }
 
-// Range of outputs along one axis whose window can reach pixel p through the border mapping.
-// Single reflections stay inside the plain window; a window wider than the image under REFLECT can
-// fold back from anywhere, so the whole axis is returned then.
+// Range of outputs along one axis whose window can reach pixel p through the border mapping (a
+// superset: callers test each candidate exactly).  REPLICATE only maps onto the edge pixels, whose
+// plain windows already hold every output that clamps onto them.  A single REFLECT fold maps the
+// unresolved position -p (top) or 2(size-1)-p (bottom) onto p; for an even window the top fold
+// reaches one output beyond the plain window, so a reachable fold extends the range to the edge.
+// A window wider than the image under REFLECT can fold back from anywhere: the whole axis.
 __device__ __forceinline__ void candidate_range(int p, int size, int k, int a, int border, int& lo, int& hi) {
     if (border == kReflect && (a > size - 1 || k - 1 - a > size - 1)) {
         lo = 0;
@@ -121,6 +124,10 @@ __device__ __forceinline__ void candidate_range(int p, int size, int k, int a, i
     }
     lo = max(p - (k - 1 - a), 0);
     hi = min(p + a, size - 1);
+    if (border == kReflect) {
+        if (p <= a) lo = 0;
+        if (2 * (size - 1) - p <= size - 1 + (k - 1 - a)) hi = size - 1;
+    }
 }
 
 // ------------------------------------------------------------------------------------------------

@@ -195,8 +195,11 @@ __global__ void __launch_bounds__(256) direct_gather_kernel(const T* __restrict_
     using G = typename GradAcc<T>::type;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int aH = kH / 2, aW = kW / 2;
-    const int rh0 = -(kH - 1 - aH), rw0 = -(kW - 1 - aW);  // halo origin relative to the tile
-    const int sw = kTile + kW - 1, sh = kTile + kH - 1;
+    // halo of aH rows / aW columns on every side: it holds every candidate output, including the one an
+    // even window reaches through a REFLECT fold beyond its plain window (see candidate_range)
+    const int rh0 = -aH, rw0 = -aW;
+    const int sw = kTile + 2 * aW, sh = kTile + 2 * aH;
+    const int offh = 2 * aH - (kH - 1), offw = 2 * aW - (kW - 1);  // 1 for an even window, else 0
     G* gs = reinterpret_cast<G*>(smem_raw);
     I* is = reinterpret_cast<I*>(gs + sw * sh);
 
@@ -255,9 +258,9 @@ __global__ void __launch_bounds__(256) direct_gather_kernel(const T* __restrict_
         if (deep) {
             // no border mapping anywhere in reach: output (ph - aH' + a, ...) selects the pixel only
             // through the tap that points straight at it
-            for (int a = 0; a < kH; ++a) {        // output row = ph + rh0 + a, ascending
+            for (int a = 0; a < kH; ++a) {        // output row = ph - (kH - 1 - aH) + a, ascending
                 const int di = kH - 1 - a;          // tap row pointing from that output to ph
-                const int srow = (lr + a) * sw + threadIdx.x;
+                const int srow = (lr + a + offh) * sw + threadIdx.x + offw;
                 for (int b = 0; b < kW; ++b) {
                     const uint32_t want = static_cast<uint32_t>(di * kW + (kW - 1 - b));
                     if (static_cast<uint32_t>(is[srow + b]) == want) acc = GradAcc<T>::add(acc, gs[srow + b]);

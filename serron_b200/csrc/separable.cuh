@@ -218,8 +218,8 @@ __global__ void __launch_bounds__(256) sep_gather_kernel(const T* __restrict__ g
     using G = typename GradAcc<T>::type;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int aH = kH / 2, aW = kW / 2;
-    const int rh0 = -(kH - 1 - aH), rw0 = -(kW - 1 - aW);
-    const int sw = kGTW + kW - 1, sh = kGTH + kH - 1;
+    const int rh0 = -aH, rw0 = -aW;  // symmetric halo: see direct_gather_kernel
+    const int sw = kGTW + 2 * aW, sh = kGTH + 2 * aH;
     G* gs = reinterpret_cast<G*>(smem_raw);
     I* is = reinterpret_cast<I*>(gs + sw * sh);
 
