@@ -14,6 +14,17 @@
 #include "segrad.cuh"
 #include "separable.cuh"
 
+namespace serron {
+// compile-time-K separable kernels, instantiated per storage type in sep_fast_<type>.cu; they return
+// 0, a cudaError_t code, or -1 when the window length has no fast path
+template <typename T>
+int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win,
+                   long long planes, int H, int W, int border, cudaStream_t stream);
+template <typename T>
+int sep_fast_gather_t(int K, const void* go, const void* win, void* gi, long long planes, int H, int W, int border,
+                      cudaStream_t stream);
+}  // namespace serron
+
 #include <algorithm>
 #include <cstdlib>
 #include <cstring>
@@ -357,6 +368,13 @@ void launch_forward_t(int algo, const Geometry& g, const void* x, const void* w,
         kernel<<<grid_1d(static_cast<long long>(tx) * ty * g.N * g.C), dim3(kTile, kTileThreadsY), smem, stream>>>(
             xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty);
     } else {
+        if constexpr (!std::is_same<T, double>::value) {
+            if (kH == kW && g.N * g.C < (1ll << 31) / 4096) {
+                const int rc = sep_fast_fwd_t<T>(OP, kH, V, X, x, y, win, g.N * g.C, H, W, border, stream);
+                if (rc > 0) SB_CUDA(static_cast<cudaError_t>(rc));
+                if (rc == 0) return;
+            }
+        }
         const int tx = ceil_div(W, kSepTW), ty = ceil_div(H, kSepTH);
         const size_t smem = SepSmem<typename Storage<T>::acc>::bytes(kH, kW);
         auto kernel = sep_fwd_kernel<T, OP, I, V, X>;
@@ -442,6 +460,17 @@ void launch_gather_t(const Geometry& g, const void* go, const void* win, void* g
     // a halo too large for shared memory walks the candidates in global memory instead
     const int force_global = smem > budget ? 1 : 0;
     if (force_global) smem = 0;
+    if constexpr (SEP && !std::is_same<T, double>::value) {
+        // the compile-time-K gather needs every candidate within a single border fold
+        const int a = kH / 2;
+        const bool single_fold = border != kReflect || (a <= H - 1 && kH - 1 - a <= H - 1 && a <= W - 1 &&
+                                                        kW - 1 - a <= W - 1);
+        if (kH == kW && single_fold && g.N * g.C < (1ll << 31) / 4096) {
+            const int rc = sep_fast_gather_t<T>(kH, go, win, gi, g.N * g.C, H, W, border, stream);
+            if (rc > 0) SB_CUDA(static_cast<cudaError_t>(rc));
+            if (rc == 0) return;
+        }
+    }
     if (SEP) {
         auto kernel = sep_gather_kernel<T, I>;
         set_smem(kernel, smem);

@@ -1,0 +1,8 @@
+// Instantiates the compile-time-K separable kernels for __nv_bfloat16 storage (see sep_fast_launch.cuh).
+#include "sep_fast_launch.cuh"
+
+namespace serron {
+template int sep_fast_fwd_t<__nv_bfloat16>(int, int, bool, bool, const void*, void*, void*, long long, int, int, int,
+                                  cudaStream_t);
+template int sep_fast_gather_t<__nv_bfloat16>(int, const void*, const void*, void*, long long, int, int, int, cudaStream_t);
+}  // namespace serron

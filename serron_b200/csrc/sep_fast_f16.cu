@@ -1,0 +1,8 @@
+// Instantiates the compile-time-K separable kernels for __half storage (see sep_fast_launch.cuh).
+#include "sep_fast_launch.cuh"
+
+namespace serron {
+template int sep_fast_fwd_t<__half>(int, int, bool, bool, const void*, void*, void*, long long, int, int, int,
+                                  cudaStream_t);
+template int sep_fast_gather_t<__half>(int, const void*, const void*, void*, long long, int, int, int, cudaStream_t);
+}  // namespace serron
