@@ -13,6 +13,7 @@
 #include "recon.cuh"
 #include "segrad.cuh"
 #include "separable.cuh"
+#include "gather_stream.cuh"
 
 namespace serron {
 // compile-time-K separable kernels, instantiated per storage type in sep_fast_<type>.cu; they return
@@ -20,9 +21,6 @@ namespace serron {
 template <typename T>
 int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win,
                    long long planes, int H, int W, int border, cudaStream_t stream);
-template <typename T>
-int sep_fast_gather_t(int K, const void* go, const void* win, void* gi, long long planes, int H, int W, int border,
-                      cudaStream_t stream);
 }  // namespace serron
 
 #include <algorithm>
@@ -261,10 +259,6 @@ bool format_is_separable(int fmt) { return fmt >= SERRON_WINNERS_SEPARABLE_U8; }
 size_t tiled_smem_bytes(int64_t kH, int64_t kW, int dtype) {
     return static_cast<size_t>((kTile + kH - 1) * (kTile + kW - 1) + kH * kW) * acc_size(dtype);
 }
-size_t gather_smem_bytes(int64_t kH, int64_t kW, int dtype, int fmt, bool sep) {
-    const int64_t tw = sep ? kGTW : kTile, th = sep ? kGTH : kTile;
-    return static_cast<size_t>((tw + 2 * (kW / 2)) * (th + 2 * (kH / 2))) * (acc_size(dtype) + format_bytes(fmt)) + 16;
-}
 size_t sep_smem_bytes(int64_t kH, int64_t kW, int dtype) {
     return dtype == kF64 ? SepSmem<double>::bytes(static_cast<int>(kH), static_cast<int>(kW))
                          : SepSmem<float>::bytes(static_cast<int>(kH), static_cast<int>(kW));
@@ -369,7 +363,7 @@ void launch_forward_t(int algo, const Geometry& g, const void* x, const void* w,
             xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty);
     } else {
         if constexpr (!std::is_same<T, double>::value) {
-            if (kH == kW && g.N * g.C < (1ll << 31) / 4096) {
+            if (kH == kW && g.N * g.C < (1ll << 31) / 4096 && g.H * g.W < (1ll << 31)) {
                 const int rc = sep_fast_fwd_t<T>(OP, kH, V, X, x, y, win, g.N * g.C, H, W, border, stream);
                 if (rc > 0) SB_CUDA(static_cast<cudaError_t>(rc));
                 if (rc == 0) return;
@@ -460,15 +454,27 @@ void launch_gather_t(const Geometry& g, const void* go, const void* win, void* g
     // a halo too large for shared memory walks the candidates in global memory instead
     const int force_global = smem > budget ? 1 : 0;
     if (force_global) smem = 0;
-    if constexpr (SEP && !std::is_same<T, double>::value) {
-        // the compile-time-K gather needs every candidate within a single border fold
-        const int a = kH / 2;
-        const bool single_fold = border != kReflect || (a <= H - 1 && kH - 1 - a <= H - 1 && a <= W - 1 &&
-                                                        kW - 1 - a <= W - 1);
-        if (kH == kW && single_fold && g.N * g.C < (1ll << 31) / 4096) {
-            const int rc = sep_fast_gather_t<T>(kH, go, win, gi, g.N * g.C, H, W, border, stream);
-            if (rc > 0) SB_CUDA(static_cast<cudaError_t>(rc));
-            if (rc == 0) return;
+    {
+        // raster-order stream gather: every candidate must lie within a single border fold
+        const bool single_fold = border != kReflect || (kH / 2 <= H - 1 && kH - 1 - kH / 2 <= H - 1 &&
+                                                        kW / 2 <= W - 1 && kW - 1 - kW / 2 <= W - 1);
+        const StreamGeom geo(kH, kW, sizeof(I));
+        const size_t stream_smem = geo.smem(sizeof(typename GradAcc<T>::type), sizeof(I));
+        if (single_fold && stream_smem <= budget && g.N * g.C < (1ll << 31) / 64) {
+            const int strips = ceil_div(W, kStreamTW);
+            const long long ctas = g.N * g.C * strips;
+            // enough single-warp CTAs to fill the machine several times over; each segment re-walks
+            // 2aH halo rows, so segments stay at least 64 rows tall
+            const long long want = std::clamp<long long>((9472 + ctas - 1) / ctas, 1, std::max(1, H / 64));
+            const int seg_h = static_cast<int>((H + want - 1) / want);
+            const int segs = ceil_div(H, seg_h);
+            auto kernel = stream_gather_kernel<T, I, SEP>;
+            set_smem(kernel, stream_smem);
+            kernel<<<grid_1d(ctas * segs), 32, stream_smem, stream>>>(
+                static_cast<const T*>(go), static_cast<const I*>(win), static_cast<T*>(gi), H, W, kH, kW, border,
+                strips, segs, seg_h);
+            SB_CUDA(cudaGetLastError());
+            return;
         }
     }
     if (SEP) {

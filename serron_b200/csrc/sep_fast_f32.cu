@@ -4,5 +4,4 @@
 namespace serron {
 template int sep_fast_fwd_t<float>(int, int, bool, bool, const void*, void*, void*, long long, int, int, int,
                                   cudaStream_t);
-template int sep_fast_gather_t<float>(int, const void*, const void*, void*, long long, int, int, int, cudaStream_t);
 }  // namespace serron

@@ -1,8 +1,10 @@
-// Host launchers of the compile-time-K separable kernels (sep_fast.cuh), instantiated once per storage
-// type in sep_fast_<type>.cu so the type variants compile in parallel.
+// Host launchers of the compile-time-K separable sweep kernels (sep_sweep.cuh), instantiated once per
+// storage type in sep_fast_<type>.cu so the type variants compile in parallel.
 #pragma once
 
-#include "sep_fast.cuh"
+#include <type_traits>
+
+#include "sep_sweep.cuh"
 
 namespace serron {
 
@@ -18,19 +20,33 @@ inline cudaError_t set_smem_attr(K_ kernel, size_t bytes) {
     return cudaSuccess;
 }
 
+// Row segments per strip: enough CTAs for ~4 waves of 148 SMs, each segment a whole number of steps.
+inline void sweep_segments(long long planes, int strips, int H, int step, int& segs, int& seg_h) {
+    const long long ctas = planes * strips;
+    const int steps = (H + step - 1) / step;
+    long long want = (592 + ctas - 1) / ctas;
+    if (want > steps) want = steps;
+    if (want < 1) want = 1;
+    const int per = static_cast<int>((steps + want - 1) / want);
+    seg_h = per * step;
+    segs = (H + seg_h - 1) / seg_h;
+}
+
 template <typename T, int OP, int K, bool V, bool X>
 int sep_fast_fwd_launch(const void* x, void* y, void* win, long long planes, int H, int W, int border,
                         cudaStream_t stream) {
-    using G = FastGeom<K>;
+    using G = SweepGeom<K, sizeof(T)>;
     using I = FastIndex<K>;
-    const int tx = (W + kFastTW - 1) / kFastTW, ty = (H + G::TH - 1) / G::TH;
-    const size_t smem = G::smem_bytes();
-    auto kernel = sep_fast_fwd_kernel<T, OP, I, V, X, K>;
+    const int strips = (W + kSweepTW - 1) / kSweepTW;
+    int segs = 1, seg_h = H;
+    sweep_segments(planes, strips, H, G::TH, segs, seg_h);
+    const size_t smem = G::fwd_smem();
+    auto kernel = sep_sweep_fwd_kernel<T, OP, I, V, X, K>;
     cudaError_t err = set_smem_attr(kernel, smem);
     if (err != cudaSuccess) return static_cast<int>(err);
-    const long long blocks = static_cast<long long>(tx) * ty * planes;
-    kernel<<<static_cast<unsigned>(blocks), kFastThreads, smem, stream>>>(
-        static_cast<const T*>(x), static_cast<T*>(y), static_cast<I*>(win), H, W, border, tx, ty);
+    const long long blocks = planes * strips * segs;
+    kernel<<<static_cast<unsigned>(blocks), kSweepThreads, smem, stream>>>(
+        static_cast<const T*>(x), static_cast<T*>(y), static_cast<I*>(win), H, W, border, strips, segs, seg_h);
     return static_cast<int>(cudaGetLastError());
 }
 
@@ -46,11 +62,11 @@ int sep_fast_fwd_k(bool with_value, bool with_index, const void* x, void* y, voi
 template <typename T>
 int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win,
                    long long planes, int H, int W, int border, cudaStream_t stream) {
-#define SERRON_SEP_FAST_FWD_CASE(k)                                                                       \
-    case k:                                                                                               \
-        return op == kErode ? sep_fast_fwd_k<T, kErode, k>(with_value, with_index, x, y, win, planes, H, W, \
-                                                           border, stream)                                \
-                            : sep_fast_fwd_k<T, kDilate, k>(with_value, with_index, x, y, win, planes, H, W, \
+#define SERRON_SEP_FAST_FWD_CASE(k)                                                                         \
+    case k:                                                                                                 \
+        return op == kErode ? sep_fast_fwd_k<T, kErode, k>(with_value, with_index, x, y, win, planes, H, W,   \
+                                                           border, stream)                                  \
+                            : sep_fast_fwd_k<T, kDilate, k>(with_value, with_index, x, y, win, planes, H, W,  \
                                                             border, stream);
     switch (K) {
         SERRON_SEP_FAST_KS(SERRON_SEP_FAST_FWD_CASE)
@@ -58,36 +74,6 @@ int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* 
         return -1;
     }
 #undef SERRON_SEP_FAST_FWD_CASE
-}
-
-template <typename T, int K>
-int sep_fast_gather_launch(const void* go, const void* win, void* gi, long long planes, int H, int W, int border,
-                           cudaStream_t stream) {
-    using G = FastGeom<K>;
-    using I = FastIndex<K>;
-    const int tx = (W + kFastTW - 1) / kFastTW, ty = (H + G::GTH - 1) / G::GTH;
-    const size_t smem = G::gather_smem_bytes(sizeof(I));
-    auto kernel = sep_fast_gather_kernel<T, I, K>;
-    cudaError_t err = set_smem_attr(kernel, smem);
-    if (err != cudaSuccess) return static_cast<int>(err);
-    const long long blocks = static_cast<long long>(tx) * ty * planes;
-    kernel<<<static_cast<unsigned>(blocks), kFastThreads, smem, stream>>>(
-        static_cast<const T*>(go), static_cast<const I*>(win), static_cast<T*>(gi), H, W, border, tx, ty);
-    return static_cast<int>(cudaGetLastError());
-}
-
-template <typename T>
-int sep_fast_gather_t(int K, const void* go, const void* win, void* gi, long long planes, int H, int W, int border,
-                      cudaStream_t stream) {
-#define SERRON_SEP_FAST_GATHER_CASE(k) \
-    case k:                            \
-        return sep_fast_gather_launch<T, k>(go, win, gi, planes, H, W, border, stream);
-    switch (K) {
-        SERRON_SEP_FAST_KS(SERRON_SEP_FAST_GATHER_CASE)
-    default:
-        return -1;
-    }
-#undef SERRON_SEP_FAST_GATHER_CASE
 }
 
 }  // namespace serron
