@@ -82,9 +82,10 @@ __global__ void __launch_bounds__(32) stream_gather_kernel(const T* __restrict__
     const bool words_ok = (static_cast<long long>(W) * sizeof(I)) % 4 == 0;
 
     const int oh_first = ph_begin - aH, oh_last = ph_end - 1 + aH;  // output rows walked
-    // stage output row oh into ring slot oh mod RR (rows outside the image: no winner, zero)
-    auto stage = [&](int oh) {
-        const int slot = ((oh % RR) + RR) % RR;
+    // ring slots advance with the row; wrap by a compare, never by a division
+    auto wrap = [](int s, int n) { return s < 0 ? s + n : (s >= n ? s - n : s); };
+    // stage output row oh into ring slot `slot` (rows outside the image: no winner, zero)
+    auto stage = [&](int oh, int slot) {
         G* gdst = gs + slot * GW;
         I* rdst = rs + slot * GWB;
         const bool row_ok = oh >= 0 && oh < H;
@@ -116,23 +117,27 @@ __global__ void __launch_bounds__(32) stream_gather_kernel(const T* __restrict__
     for (int i = lane; i < AR * kStreamTW; i += 32) acc[i] = G(0);
     // prologue: rows needed before the first one is processed (records reach aH rows below)
     int staged = oh_first - 1;  // last staged row
-    const int ahead = aH + kStreamPF;
+    const int ahead = aH + kStreamPF;  // < RR
+    int slot = ((oh_first % RR) + RR) % RR;   // ring slot of row oh
+    int aslot = ((oh_first % AR) + AR) % AR;  // accumulator slot of pixel row oh
     for (int r = oh_first; r <= min(oh_last, oh_first + ahead); ++r) {
-        stage(r);
+        stage(r, wrap(slot + (r - oh_first), RR));
         sg_commit();
         staged = r;
     }
+    // exact division of a record (< 2^16) by kW: multiply-high by ceil(2^32 / kW)
+    const uint32_t div_magic = kW > 1 ? static_cast<uint32_t>(((1ull << 32) + kW - 1) / kW) : 0u;
 
     for (int oh = oh_first; oh <= oh_last; ++oh) {
         // keep the ring filled `ahead` rows past oh; rows up to oh + aH must have landed
         if (staged < oh_last && staged < oh + ahead) {
-            stage(++staged);
+            ++staged;
+            stage(staged, wrap(slot + (staged - oh), RR));
         }
         sg_commit();
         sg_wait<kStreamPF>();
         __syncwarp();
 
-        const int slot = ((oh % RR) + RR) % RR;
         const G* grow = gs + slot * GW;
         const I* rrow = rs + slot * GWB + roff;
         for (int q0 = 0; q0 < GW; q0 += 32) {
@@ -147,7 +152,7 @@ __global__ void __launch_bounds__(32) stream_gather_kernel(const T* __restrict__
                     if (hi != sep_none_hi<I>()) {
                         r = oh + static_cast<int>(hi) - aH;
                         if (resolve(r, H, border) && r >= ph_begin && r < ph_end) {
-                            const int rslot = ((r % RR) + RR) % RR;
+                            const int rslot = wrap(slot + (r - oh), RR);  // |r - oh| <= aH
                             c = ow + static_cast<int>(sep_lo<I>(rs[rslot * GWB + roff + q])) - aW;
                             if (!resolve(c, W, border)) r = -1;
                         } else {
@@ -155,11 +160,13 @@ __global__ void __launch_bounds__(32) stream_gather_kernel(const T* __restrict__
                         }
                     }
                 } else if (v != IndexTraits<I>::none) {
-                    r = oh + static_cast<int>(v / static_cast<uint32_t>(kW)) - aH;
-                    c = ow + static_cast<int>(v % static_cast<uint32_t>(kW)) - aW;
+                    const uint32_t di = sizeof(I) <= 2 ? (kW > 1 ? __umulhi(v, div_magic) : v)
+                                                       : v / static_cast<uint32_t>(kW);
+                    r = oh + static_cast<int>(di) - aH;
+                    c = ow + static_cast<int>(v - di * static_cast<uint32_t>(kW)) - aW;
                     if (!resolve(r, H, border) || !resolve(c, W, border) || r < ph_begin || r >= ph_end) r = -1;
                 }
-                if (r >= 0 && c >= pw0 && c < pw0 + kStreamTW) key = (((r % AR) + AR) % AR) * kStreamTW + (c - pw0);
+                if (r >= 0 && c >= pw0 && c < pw0 + kStreamTW) key = wrap(aslot + (r - oh), AR) * kStreamTW + (c - pw0);
             }
             const unsigned group = __match_any_sync(0xffffffffu, key);
             if (key >= 0 && lane == __ffs(group) - 1) {
@@ -177,7 +184,7 @@ __global__ void __launch_bounds__(32) stream_gather_kernel(const T* __restrict__
         // pixel row oh - aH is complete: write it and free its slot
         const int done = oh - aH;
         if (done >= ph_begin && done < ph_end) {
-            G* arow = acc + (((done % AR) + AR) % AR) * kStreamTW;
+            G* arow = acc + wrap(aslot - aH, AR) * kStreamTW;
             for (int c = lane; c < kStreamTW; c += 32) {
                 if (pw0 + c < W)
                     gip[static_cast<long long>(done) * W + pw0 + c] =
@@ -186,6 +193,8 @@ __global__ void __launch_bounds__(32) stream_gather_kernel(const T* __restrict__
             }
         }
         __syncwarp();
+        slot = wrap(slot + 1, RR);
+        aslot = wrap(aslot + 1, AR);
     }
     sg_wait<0>();
 }
