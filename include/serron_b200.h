@@ -176,6 +176,29 @@ SERRON_API int serron_reconstruct(int32_t dilate, const void* marker, const void
 SERRON_API int64_t serron_reconstruct_workspace_bytes(const int64_t* sizes, int64_t dim, int32_t dtype,
                                                       int64_t max_iter);
 
+/* ---------------------------------------------------------------------------------------------
+ * Backward without any allocation.  No counterpart in the reference (its backward allocates its own
+ * temporaries through torch); this is an addition for callers that cannot allocate device memory: a
+ * host binding this ABI that owns only its input and output buffers, or one that must not call
+ * cudaMalloc / cudaFree between launches (they synchronise the device and can fail under a fixed
+ * memory budget).
+ *
+ * Same arguments and results as serron_erode_backward / serron_dilate_backward (`op` selects which),
+ * with the workspace taken from a fixed array of SERRON_STATIC_SCRATCH_BYTES per device that the
+ * library reserves when it loads on that device.  A call needing more is rejected with
+ * SERRON_ERR_WORKSPACE before anything is enqueued.  The first call on a device looks the array up
+ * and may load the library's module there: make it before any stream capture.  All calls on a device
+ * share the array, so calls that can overlap on the GPU (two streams, two host threads) race: order
+ * them on one stream or with events.  Nothing in the array needs clearing between calls.
+ * --------------------------------------------------------------------------------------------- */
+#define SERRON_STATIC_SCRATCH_BYTES (32ll << 20)
+SERRON_API int serron_backward_static_scratch(int32_t op, const void* grad_output, const int64_t* grad_output_sizes,
+                                              int64_t grad_output_dim, const void* input, const int64_t* input_sizes,
+                                              int64_t input_dim, const void* kernel, const int64_t* kernel_sizes,
+                                              int64_t kernel_dim, int32_t dtype, int64_t border, int32_t flat,
+                                              int32_t need_kernel_grad, int64_t algo, void* grad_input,
+                                              void* grad_kernel, int32_t device, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

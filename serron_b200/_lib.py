@@ -48,6 +48,7 @@ EXPORTED = (
     "serron_get_separable_min_k",
     "serron_reconstruct",
     "serron_reconstruct_workspace_bytes",
+    "serron_backward_static_scratch",
 )
 
 
@@ -114,6 +115,8 @@ def load() -> ctypes.CDLL:
         lib.serron_reconstruct.restype = ctypes.c_int
         lib.serron_reconstruct_workspace_bytes.argtypes = [p64, i64, i32, i64]
         lib.serron_reconstruct_workspace_bytes.restype = i64
+        lib.serron_backward_static_scratch.argtypes = [i32] + bwd[:14] + [vp, vp, i32, vp]
+        lib.serron_backward_static_scratch.restype = ctypes.c_int
         _lib = lib
         return lib
 

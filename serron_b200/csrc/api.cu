@@ -719,6 +719,10 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
 }
 
 }  // namespace
+
+// Lets the library's other translation units report a failure through serron_last_error.
+void set_last_error(const std::string& message) { g_last_error = message; }
+
 }  // namespace serron
 
 using namespace serron;
