@@ -58,7 +58,10 @@ extern "C" {
 #define SERRON_ERODE 0
 #define SERRON_DILATE 1
 
-/* winner-record formats (one record per output, written by serron_forward) */
+/* winner-record formats (one record per output).  serron_forward writes the direct formats for every
+ * algorithm: t = di * kW + dj of the winning SE cell, all ones when the window has no winner.  The
+ * separable formats (hi = di, lo = dj of the output's own row) are accepted by
+ * serron_backward_from_winners. */
 #define SERRON_WINNERS_NONE 0
 #define SERRON_WINNERS_DIRECT_U8 1
 #define SERRON_WINNERS_DIRECT_U16 2

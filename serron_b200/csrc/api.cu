@@ -13,6 +13,7 @@
 #include "recon.cuh"
 #include "segrad.cuh"
 #include "separable.cuh"
+#include "gather_pull.cuh"
 #include "gather_stream.cuh"
 
 namespace serron {
@@ -296,9 +297,8 @@ int resolve_algorithm(int requested, const Problem& p, const char* name) {
         return kSeparable;
     }
 }
-int winners_format_for(int algo, int64_t kH, int64_t kW) {
-    return algo == kSeparable ? separable_format(kH, kW) : direct_format(kH, kW);
-}
+// every forward algorithm writes direct taps; the packed separable formats are accepted as input only
+int winners_format_for(int /*algo*/, int64_t kH, int64_t kW) { return direct_format(kH, kW); }
 
 // ------------------------------------------------------------------------------------------------
 // type dispatch
@@ -455,9 +455,34 @@ void launch_gather_t(const Geometry& g, const void* go, const void* win, void* g
     const int force_global = smem > budget ? 1 : 0;
     if (force_global) smem = 0;
     {
-        // raster-order stream gather: every candidate must lie within a single border fold
+        // strip pull and raster-order stream gathers: every candidate must lie within a single border fold
         const bool single_fold = border != kReflect || (kH / 2 <= H - 1 && kH - 1 - kH / 2 <= H - 1 &&
                                                         kW / 2 <= W - 1 && kW - 1 - kW / 2 <= W - 1);
+        if (!SEP && single_fold && PullGeom::taps_fit(kH, kW, sizeof(I))) {
+            const PullGeom geo(kH, kW, sizeof(T), sizeof(I));
+            const size_t pull_smem = geo.smem();
+            const int strips = ceil_div(W, kPullTQ);
+            const long long ctas = g.N * g.C * strips;
+            if (pull_smem <= budget && ctas < (1ll << 31) / 64) {
+                // enough CTAs for several waves; each segment re-reads 2aH rows, so keep them >= 4 bands
+                const long long want = std::clamp<long long>((2400 + ctas - 1) / ctas, 1, std::max(1, H / (4 * kPullTB)));
+                const int seg_h = static_cast<int>((H + want - 1) / want);
+                const int segs = ceil_div(H, seg_h);
+                auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+                const int go_vec = aligned(go) && (W * sizeof(T)) % 16 == 0;
+                const int rec_vec = aligned(win) && (W * sizeof(I)) % 16 == 0;
+                const int out_vec = aligned(gi) && (W * sizeof(T)) % 16 == 0;
+                auto kernel = pull_gather_kernel<T, I>;
+                set_smem(kernel, pull_smem);
+                // four CTAs per SM need the largest shared-memory carveout
+                SB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+                kernel<<<grid_1d(ctas * segs), kPullThreads, pull_smem, stream>>>(
+                    static_cast<const T*>(go), static_cast<const I*>(win), static_cast<T*>(gi), H, W, kH, kW, border,
+                    strips, segs, seg_h, go_vec, rec_vec, out_vec);
+                SB_CUDA(cudaGetLastError());
+                return;
+            }
+        }
         const StreamGeom geo(kH, kW, sizeof(I));
         const size_t stream_smem = geo.smem(sizeof(typename GradAcc<T>::type), sizeof(I));
         if (single_fold && stream_smem <= budget && g.N * g.C < (1ll << 31) / 64) {

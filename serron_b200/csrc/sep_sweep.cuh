@@ -9,7 +9,8 @@
 //                chunk, a prefix arg-scan over the next chunk, one compare-select per output to combine
 //                (van Herk / Gil-Werman: three compare-selects per output, any K);
 //   column pass  the same over the row results.
-// grad_input for the records it writes is formed by the ordered-ownership gather (gather_band.cuh).
+// With a winner buffer every output gets the direct tap di * K + dj of its winner (di from the column
+// pass, dj from the row pass of the winning row), the record the direct kernels write.
 #pragma once
 
 #include "common.cuh"
@@ -207,14 +208,16 @@ __global__ void __launch_bounds__(kSweepThreads) sep_sweep_fwd_kernel(const T* _
             const int o0 = (s0 + base) * W + ow;
             T* yp = y + plane * H * W;
             I* wp = win + plane * H * W;
-            const uint8_t* lo_col = rdj + (base + a) * RS + j;
+            const uint8_t* dj_col = rdj + base * RS + j;
             sweep_run<K, OP, WITH_INDEX>(v, [&](int m, float val, int off) {
                 if (base + m < rows_left) {
                     const int o = o0 + m * W;
                     if (WITH_VALUE) yp[o] = Storage<T>::store(val);
                     if (WITH_INDEX) {
-                        const uint32_t hi = val == neutral ? sep_none_hi<I>() : static_cast<uint32_t>(off);
-                        wp[o] = static_cast<I>((hi << IndexTraits<I>::half_bits) | lo_col[m * RS]);
+                        // winning row base + m + off, and the column its own row pass chose
+                        const uint32_t t = val == neutral ? IndexTraits<I>::none
+                                                          : static_cast<uint32_t>(off) * K + dj_col[(m + off) * RS];
+                        wp[o] = static_cast<I>(t);
                     }
                 }
             });

@@ -7,8 +7,8 @@
 // first extremum and the column keeps the first row).
 //
 // B200 layout: one CTA owns a TH x TW output tile and runs both passes out of shared memory, so the
-// row result never goes to HBM.  With a winner buffer the tile also writes one packed record per
-// output: hi = column winner di, lo = the row winner dj of the output's own row (see common.cuh).
+// row result never goes to HBM.  With a winner buffer the tile also writes the direct tap
+// di * kW + dj of every output's winner (di from the column pass, dj from the winning row's row pass).
 #pragma once
 
 #include "common.cuh"
@@ -191,9 +191,11 @@ __global__ void __launch_bounds__(kSepThreads) sep_fwd_kernel(const T* __restric
                 const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
                 if (WITH_VALUE) y[o] = Storage<T>::store(bv);
                 if (WITH_INDEX) {
-                    const uint32_t hi = bv == neutral ? sep_none_hi<I>() : static_cast<uint32_t>(bi - i);
-                    const uint32_t lo = rdj[(i + aH) * kSepTW + j];
-                    win[o] = static_cast<I>((hi << IndexTraits<I>::half_bits) | lo);
+                    // direct tap of the winner: row bi of the row results, column from its row pass
+                    const uint32_t t = bv == neutral ? IndexTraits<I>::none
+                                                     : static_cast<uint32_t>(bi - i) * static_cast<uint32_t>(kW) +
+                                                           rdj[bi * kSepTW + j];
+                    win[o] = static_cast<I>(t);
                 }
             }
         }
