@@ -400,7 +400,8 @@ void launch_forward(int op, int dtype, int algo, const Geometry& g, const void* 
     });
 }
 
-// backward workspace layout: [winners][segrad partials][segrad global bins], each 256-byte aligned
+// backward workspace layout: [winners][segrad partials][segrad global bins][target map], each 256-byte
+// aligned; the winners only when the backward computes them, the segrad parts only for grad_kernel
 struct SegradPlan {
     int chunks = 0;
     int threads = 0;
@@ -430,19 +431,22 @@ SegradPlan segrad_plan(const Geometry& g) {
 }
 int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
 
+int64_t segrad_workspace(const Geometry& g, bool need_kg) {
+    if (!need_kg) return 0;
+    const SegradPlan p = segrad_plan(g);
+    return align256(p.partial_bytes) + align256(p.bins_bytes);
+}
+int64_t map_workspace(const Geometry& g) { return align256(pull_map_words(g.N * g.C, g.H, g.W) * 4); }
+
 int64_t backward_workspace(const Geometry& g, bool need_kg, int fmt, bool with_winners) {
     int64_t bytes = 0;
     if (!with_winners) bytes += align256(g.numel() * format_bytes(fmt));
-    if (need_kg) {
-        const SegradPlan p = segrad_plan(g);
-        bytes += align256(p.partial_bytes) + align256(p.bins_bytes);
-    }
-    return bytes;
+    return bytes + segrad_workspace(g, need_kg) + map_workspace(g);
 }
 
 template <typename T, typename I, bool SEP>
-void launch_gather_t(const Geometry& g, const void* go, const void* win, void* gi, int border, size_t budget,
-                     cudaStream_t stream) {
+void launch_gather_t(const Geometry& g, const void* go, const void* win, void* gi, uint32_t* map, int border,
+                     size_t budget, cudaStream_t stream) {
     const int H = static_cast<int>(g.H), W = static_cast<int>(g.W);
     const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW);
     const int dtype = std::is_same<T, double>::value ? kF64 : kF32;
@@ -455,30 +459,39 @@ void launch_gather_t(const Geometry& g, const void* go, const void* win, void* g
     const int force_global = smem > budget ? 1 : 0;
     if (force_global) smem = 0;
     {
-        // strip pull and raster-order stream gathers: every candidate must lie within a single border fold
+        // mark-and-pull and raster-order stream gathers: every candidate must lie within a single border fold
         const bool single_fold = border != kReflect || (kH / 2 <= H - 1 && kH - 1 - kH / 2 <= H - 1 &&
                                                         kW / 2 <= W - 1 && kW - 1 - kW / 2 <= W - 1);
-        if (!SEP && single_fold && PullGeom::taps_fit(kH, kW, sizeof(I))) {
-            const PullGeom geo(kH, kW, sizeof(T), sizeof(I));
-            const size_t pull_smem = geo.smem();
+        if (!SEP && single_fold && map != nullptr && pull_taps_fit(kH, kW, sizeof(I))) {
+            const PullGeom geo(kH, kW, sizeof(I));
+            const size_t mark_smem = geo.smem();
             const int strips = ceil_div(W, kPullTQ);
             const long long ctas = g.N * g.C * strips;
-            if (pull_smem <= budget && ctas < (1ll << 31) / 64) {
+            const SumGeom sgeo_check(kH, kW, sizeof(T), sizeof(I));
+            if (mark_smem <= budget && sgeo_check.smem() <= budget && ctas < (1ll << 31) / 64 &&
+                g.N * g.C * ceil_div(W, kPullTQ) * static_cast<long long>(ceil_div(H, kSumTP)) < (1ll << 31)) {
                 // enough CTAs for several waves; each segment re-reads 2aH rows, so keep them >= 4 bands
                 const long long want = std::clamp<long long>((2400 + ctas - 1) / ctas, 1, std::max(1, H / (4 * kPullTB)));
                 const int seg_h = static_cast<int>((H + want - 1) / want);
                 const int segs = ceil_div(H, seg_h);
                 auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-                const int go_vec = aligned(go) && (W * sizeof(T)) % 16 == 0;
                 const int rec_vec = aligned(win) && (W * sizeof(I)) % 16 == 0;
                 const int out_vec = aligned(gi) && (W * sizeof(T)) % 16 == 0;
-                auto kernel = pull_gather_kernel<T, I>;
-                set_smem(kernel, pull_smem);
-                // four CTAs per SM need the largest shared-memory carveout
-                SB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-                kernel<<<grid_1d(ctas * segs), kPullThreads, pull_smem, stream>>>(
-                    static_cast<const T*>(go), static_cast<const I*>(win), static_cast<T*>(gi), H, W, kH, kW, border,
-                    strips, segs, seg_h, go_vec, rec_vec, out_vec);
+                auto mark = pull_mark_kernel<T, I>;
+                set_smem(mark, mark_smem);
+                mark<<<grid_1d(ctas * segs), kPullThreads, mark_smem, stream>>>(
+                    static_cast<const I*>(win), static_cast<T*>(gi), map, H, W, kH, kW, border, strips, segs, seg_h,
+                    rec_vec, out_vec);
+                SB_CUDA(cudaGetLastError());
+                const SumGeom sgeo(kH, kW, sizeof(T), sizeof(I));
+                const int tiles_x = ceil_div(W, kPullTQ), tiles_y = ceil_div(H, kSumTP);
+                const int go_vec = aligned(go) && (W * sizeof(T)) % 16 == 0;
+                auto sum = pull_sum_kernel<T, I>;
+                set_smem(sum, sgeo.smem());
+                SB_CUDA(cudaFuncSetAttribute(sum, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+                sum<<<grid_1d(g.N * g.C * tiles_x * tiles_y), kSumThreads, sgeo.smem(), stream>>>(
+                    static_cast<const T*>(go), static_cast<const I*>(win), map, static_cast<T*>(gi), H, W, kH, kW,
+                    border, tiles_x, tiles_y, go_vec, rec_vec);
                 SB_CUDA(cudaGetLastError());
                 return;
             }
@@ -545,14 +558,15 @@ void launch_backward_from_winners(int op, int dtype, const Geometry& g, const vo
                                   void* gi, void* gk, bool need_kg, void* ws, int border, size_t budget,
                                   cudaStream_t stream) {
     const bool sep = format_is_separable(fmt);
+    uint32_t* map = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + segrad_workspace(g, need_kg));
     dispatch_dtype(dtype, [&](auto t) {
         using T = decltype(t);
         dispatch_index(fmt, [&](auto i) {
             using I = decltype(i);
             if (sep)
-                launch_gather_t<T, I, true>(g, go, win, gi, border, budget, stream);
+                launch_gather_t<T, I, true>(g, go, win, gi, map, border, budget, stream);
             else
-                launch_gather_t<T, I, false>(g, go, win, gi, border, budget, stream);
+                launch_gather_t<T, I, false>(g, go, win, gi, map, border, budget, stream);
             if (need_kg) {
                 if (sep)
                     launch_segrad_t<T, I, true>(op, g, go, win, gk, ws, border, stream);

@@ -86,8 +86,9 @@ def test_workspace_sizes_are_deterministic(lib):
     ks, kd = _lib.sizes((15, 15))
     with_w = lib.serron_backward_workspace_bytes(xs, xd, ks, kd, 0, 4, 1)
     without = lib.serron_backward_workspace_bytes(xs, xd, ks, kd, 0, 4, 0)
-    assert with_w == 0
-    assert without == 32 * 64 * 512 * 512  # one byte per output for the separable u8 record
+    target_map = 32 * 64 * 512 * (512 // 32) * 4  # one bit per pixel
+    assert with_w == target_map
+    assert without == 32 * 64 * 512 * 512 + target_map  # and one byte per output for the u8 record
     assert lib.serron_reconstruct_workspace_bytes(xs, xd, 0, 0) == 256
 
 
