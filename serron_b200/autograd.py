@@ -51,7 +51,8 @@ def _forward(ctx, op: int, input_: torch.Tensor, kernel: torch.Tensor, border: i
     x, k = input_, kernel
     if input_.is_cuda and torch.is_autocast_enabled("cuda"):
         x, k = _autocast_cast(input_), _autocast_cast(kernel)
-    wants_grad = torch.is_grad_enabled() and any(ctx.needs_input_grad[:2])
+    # grad mode is off inside Function.forward; needs_input_grad says whether a backward can follow
+    wants_grad = any(ctx.needs_input_grad[:2])
     if wants_grad and x.dtype == input_.dtype and input_.is_cuda and kernel.is_cuda:
         y, ctx.winners, ctx.winners_format = _ops.forward_with_winners(op, x, k, border, flat, algo)
         return y

@@ -168,15 +168,12 @@ __global__ void __launch_bounds__(kPullThreads, 4) pull_mark_kernel(const I* __r
                     markS[ms * TQ + yc] = 1;
                 }
             };
-            // every target of these rows in this strip lies inside the image: no folding
-            const bool inside =
-                decoded - aH >= 0 && need - 1 + aH <= H - 1 && c0 - 2 * aW >= 0 && c0 + TQ + 2 * aW <= W;
             const int nrows = need - decoded;
             const int slot_d = (decoded - hbase) % RR;
-            if (sizeof(I) == 1 && inside) {
+            if constexpr (sizeof(I) == 1) {
                 // (row, word) items, four records per word.  The words span tap columns [0, hq) and a few
-                // real neighbours, whose targets fall outside the strip.  A "none" record decodes to a
-                // pixel that no record selects: marking it costs one sum of no terms, so it is kept.
+                // real neighbours, whose targets (folded or not) fall outside the strip; staged columns
+                // outside the image hold "none".  Only outputs near the image edge take the fold branch.
                 const int wfirst = roff >> 2, nwords = ((roff + hq - 1) >> 2) - wfirst + 1;
                 const uint32_t nw_magic = static_cast<uint32_t>(((1ull << 32) + nwords - 1) / nwords);
                 const uint32_t* tw = reinterpret_cast<const uint32_t*>(recS);
@@ -187,13 +184,20 @@ __global__ void __launch_bounds__(kPullThreads, 4) pull_mark_kernel(const I* __r
                     int slot = slot_d + r;
                     if (slot >= RR) slot -= RR;
                     const uint32_t word = tw[slot * rqw + wfirst + q];
-                    const int xb = decoded + r - aH;                 // target row = xb + di
-                    const int yb = 4 * (wfirst + q) - roff - 2 * aW;  // target column - c0 = yb + e + dj
+                    const int h = decoded + r;
+                    const int wb = c0 - aW + 4 * (wfirst + q) - roff;  // image column of byte 0
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         const uint32_t t = (word >> (8 * e)) & 0xffu;
+                        if (t == 0xffu) continue;
                         const uint32_t di = kW > 1 ? __umulhi(t, kw_magic) : t;
-                        mark(xb + static_cast<int>(di), yb + e + static_cast<int>(t - di * static_cast<uint32_t>(kW)));
+                        int x = h + static_cast<int>(di) - aH;
+                        int y = wb + e + static_cast<int>(t - di * static_cast<uint32_t>(kW)) - aW;
+                        if (static_cast<unsigned>(x) >= static_cast<unsigned>(H) ||
+                            static_cast<unsigned>(y) >= static_cast<unsigned>(W)) {
+                            if (!fold1(x, H, border) || !fold1(y, W, border)) continue;  // CONSTANT pad
+                        }
+                        mark(x, y - c0);
                     }
                 }
             } else {
@@ -446,6 +450,8 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
             const int r = static_cast<int>(__umulhi(static_cast<uint32_t>(i), mq)), lw = i - r * hq;
             const int h = lo + r, w = c0 - aW + lw;
             if (static_cast<unsigned>(w) >= static_cast<unsigned>(W)) continue;
+            // an odd window inside the image selects a pixel inside it: its record is its box tap
+            if ((kW & 1) && h >= aH && h < H - aH && w >= aW && w < W - aW) continue;
             I& rec = recS[(h - (r0 - aH)) * rq + roff + lw];
             int x, y;
             if (!pg_target(rec, kNone, h, w, H, W, kW, aH, aW, border, kw_magic, x, y))
