@@ -69,11 +69,17 @@ extern "C" {
 #define SERRON_WINNERS_SEPARABLE_U8 4
 #define SERRON_WINNERS_SEPARABLE_U16 5
 #define SERRON_WINNERS_SEPARABLE_U32 6
+/* Flag on a direct format: the record buffer also carries the gather's target map (one bit per pixel
+ * that wins some window; rows of ceil(W/32) 32-bit words, planes one after the other), starting at the
+ * first 256-byte boundary after the records.  serron_forward fills it; serron_backward_from_winners
+ * then skips finding the winners again.  Size of such a buffer: serron_winners_bytes. */
+#define SERRON_WINNERS_MAP 0x10
 
 /* How the library will run one call. */
 typedef struct serron_plan_t {
     int32_t algo;                /* resolved algorithm: 1 element, 2 tiled, 3 separable */
-    int32_t winners_format;      /* SERRON_WINNERS_* of the records serron_forward writes */
+    int32_t winners_format;      /* SERRON_WINNERS_* of the records serron_forward writes (with the map flag
+                                    where the gather can use a target map) */
     int32_t winners_bytes;       /* bytes per output of that record (1, 2 or 4) */
     int32_t reserved;
     int64_t workspace_bytes;     /* backward: device workspace needed when no winner records are given */
@@ -115,6 +121,10 @@ SERRON_API int serron_forward(int32_t op, const void* input, const int64_t* inpu
                               const void* kernel, const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype,
                               int64_t border, int32_t flat, int64_t algo, void* output, void* winners,
                               int32_t winners_format, int32_t device, void* stream);
+/* Bytes of a record buffer of `winners_format` for an input of `sizes` (4-D): one record per output,
+ * plus the target map when the format carries SERRON_WINNERS_MAP; -1 for bad arguments.  No
+ * reference counterpart (the reference keeps no winner records). */
+SERRON_API int64_t serron_winners_bytes(const int64_t* sizes, int64_t dim, int32_t winners_format);
 
 /* ---------------------------------------------------------------------------------------------
  * Backward.  Replaces serron::erode_backward / serron::dilate_backward

@@ -26,6 +26,7 @@ ERODE, DILATE = 0, 1
 DTYPE_CODE = {torch.float32: 0, torch.float64: 1, torch.float16: 2, torch.bfloat16: 3}
 
 WINNERS_NONE = 0
+WINNERS_MAP = 0x10  # flag: the record buffer also carries the gather's target map
 WINNERS_BYTES = {1: 1, 2: 2, 3: 4, 4: 1, 5: 2, 6: 4}
 WINNERS_TORCH_DTYPE = {1: torch.uint8, 2: torch.uint16, 3: torch.uint32, 4: torch.uint8, 5: torch.uint16,
                        6: torch.uint32}
@@ -49,6 +50,7 @@ EXPORTED = (
     "serron_reconstruct",
     "serron_reconstruct_workspace_bytes",
     "serron_backward_static_scratch",
+    "serron_winners_bytes",
 )
 
 
@@ -117,6 +119,8 @@ def load() -> ctypes.CDLL:
         lib.serron_reconstruct_workspace_bytes.restype = i64
         lib.serron_backward_static_scratch.argtypes = [i32] + bwd[:14] + [vp, vp, i32, vp]
         lib.serron_backward_static_scratch.restype = ctypes.c_int
+        lib.serron_winners_bytes.argtypes = [p64, i64, i32]
+        lib.serron_winners_bytes.restype = i64
         _lib = lib
         return lib
 

@@ -95,8 +95,15 @@ def forward_with_winners(op: int, input_: torch.Tensor, kernel: torch.Tensor, bo
     k = kernel.contiguous()
     p = plan(x, k, flat, algo, backward=False)
     out = torch.empty_like(x)
-    winners = torch.empty(x.shape, dtype=_lib.WINNERS_TORCH_DTYPE[p.winners_format], device=x.device)
     xs, xd = _lib.sizes(x.shape)
+    if p.winners_format & _lib.WINNERS_MAP:
+        # one byte buffer: the records, then the gather's target map
+        nbytes = _lib.load().serron_winners_bytes(xs, xd, p.winners_format)
+        if nbytes < 0:
+            _lib.raise_for(_lib.ERR_INVALID)
+        winners = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    else:
+        winners = torch.empty(x.shape, dtype=_lib.WINNERS_TORCH_DTYPE[p.winners_format], device=x.device)
     ks, kd = _lib.sizes(k.shape)
     # the plan resolved the algorithm; a forced separable launch needs the flatness it was resolved with
     rc = _lib.load().serron_forward(op, x.data_ptr(), xs, xd, k.data_ptr(), ks, kd, _lib.DTYPE_CODE[x.dtype],

@@ -18,9 +18,10 @@
 
 namespace serron {
 // compile-time-K separable kernels, instantiated per storage type in sep_fast_<type>.cu; they return
-// 0, a cudaError_t code, or -1 when the window length has no fast path
+// 0, a cudaError_t code, or -1 when the window length has no fast path; with `map` they also set the
+// winners in the gather's target map
 template <typename T>
-int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win,
+int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win, uint32_t* map,
                    long long planes, int H, int W, int border, cudaStream_t stream);
 }  // namespace serron
 
@@ -244,8 +245,10 @@ int separable_format(int64_t kH, int64_t kW) {
     if (kH <= 255 && kW <= 256) return SERRON_WINNERS_SEPARABLE_U16;
     return SERRON_WINNERS_SEPARABLE_U32;
 }
+int base_format(int fmt) { return fmt & ~SERRON_WINNERS_MAP; }
+bool format_has_map(int fmt) { return (fmt & SERRON_WINNERS_MAP) != 0; }
 int format_bytes(int fmt) {
-    switch (fmt) {
+    switch (base_format(fmt)) {
     case SERRON_WINNERS_DIRECT_U8:
     case SERRON_WINNERS_SEPARABLE_U8: return 1;
     case SERRON_WINNERS_DIRECT_U16:
@@ -255,7 +258,7 @@ int format_bytes(int fmt) {
     default: return 0;
     }
 }
-bool format_is_separable(int fmt) { return fmt >= SERRON_WINNERS_SEPARABLE_U8; }
+bool format_is_separable(int fmt) { return base_format(fmt) >= SERRON_WINNERS_SEPARABLE_U8; }
 
 size_t tiled_smem_bytes(int64_t kH, int64_t kW, int dtype) {
     return static_cast<size_t>((kTile + kH - 1) * (kTile + kW - 1) + kH * kW) * acc_size(dtype);
@@ -297,8 +300,12 @@ int resolve_algorithm(int requested, const Problem& p, const char* name) {
         return kSeparable;
     }
 }
-// every forward algorithm writes direct taps; the packed separable formats are accepted as input only
-int winners_format_for(int /*algo*/, int64_t kH, int64_t kW) { return direct_format(kH, kW); }
+// every forward algorithm writes direct taps, with the gather's target map where the gather can use one;
+// the packed separable formats are accepted as input only
+int winners_format_for(int /*algo*/, int64_t kH, int64_t kW) {
+    const int fmt = direct_format(kH, kW);
+    return pull_taps_fit(kH, kW, format_bytes(fmt)) ? fmt | SERRON_WINNERS_MAP : fmt;
+}
 
 // ------------------------------------------------------------------------------------------------
 // type dispatch
@@ -341,9 +348,10 @@ unsigned int grid_1d(long long blocks) {
 // ------------------------------------------------------------------------------------------------
 // launches
 // ------------------------------------------------------------------------------------------------
+// Returns true when the launch also filled `map` (the separable sweep does, for its window lengths).
 template <typename T, int OP, typename I, bool V, bool X>
-void launch_forward_t(int algo, const Geometry& g, const void* x, const void* w, void* y, void* win, int border,
-                      cudaStream_t stream) {
+bool launch_forward_t(int algo, const Geometry& g, const void* x, const void* w, void* y, void* win, uint32_t* map,
+                      int border, cudaStream_t stream) {
     const int H = static_cast<int>(g.H), W = static_cast<int>(g.W), C = static_cast<int>(g.C);
     const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW), kcs = static_cast<int>(g.kcs);
     const T* xp = static_cast<const T*>(x);
@@ -364,9 +372,10 @@ void launch_forward_t(int algo, const Geometry& g, const void* x, const void* w,
     } else {
         if constexpr (!std::is_same<T, double>::value) {
             if (kH == kW && g.N * g.C < (1ll << 31) / 4096 && g.H * g.W < (1ll << 31)) {
-                const int rc = sep_fast_fwd_t<T>(OP, kH, V, X, x, y, win, g.N * g.C, H, W, border, stream);
+                const int rc = sep_fast_fwd_t<T>(OP, kH, V, X, x, y, win, X ? map : nullptr, g.N * g.C, H, W, border,
+                                                 stream);
                 if (rc > 0) SB_CUDA(static_cast<cudaError_t>(rc));
-                if (rc == 0) return;
+                if (rc == 0) return X && map != nullptr;
             }
         }
         const int tx = ceil_div(W, kSepTW), ty = ceil_div(H, kSepTH);
@@ -377,31 +386,85 @@ void launch_forward_t(int algo, const Geometry& g, const void* x, const void* w,
             xp, yp, ip, H, W, kH, kW, border, tx, ty);
     }
     SB_CUDA(cudaGetLastError());
+    return false;
 }
 
+int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
+int64_t map_workspace(const Geometry& g) { return align256(pull_map_words(g.N * g.C, g.H, g.W) * 4); }
+// a record buffer with the map flag: the records, then the map from the next 256-byte boundary
+int64_t records_bytes(const Geometry& g, int fmt) { return align256(g.numel() * format_bytes(fmt)); }
+int64_t winners_buffer_bytes(const Geometry& g, int fmt) {
+    return format_has_map(fmt) ? records_bytes(g, fmt) + map_workspace(g) : g.numel() * format_bytes(fmt);
+}
+
+// The mark-and-pull gather applies: candidates within one border fold, box taps that fit the record,
+// and both of its kernels within the shared-memory budget and the grid limits.
+bool pull_applicable(const Geometry& g, int border, size_t elem, int idx, size_t budget) {
+    const int64_t H = g.H, W = g.W, kH = g.kH, kW = g.kW;
+    const bool single_fold =
+        border != kReflect || (kH / 2 <= H - 1 && kH - 1 - kH / 2 <= H - 1 && kW / 2 <= W - 1 && kW - 1 - kW / 2 <= W - 1);
+    if (!single_fold || !pull_taps_fit(kH, kW, idx)) return false;
+    const PullGeom mg(static_cast<int>(kH), static_cast<int>(kW), idx);
+    const SumGeom sg(static_cast<int>(kH), static_cast<int>(kW), static_cast<int>(elem), idx);
+    const long long strips = (W + kPullTQ - 1) / kPullTQ, bands = (H + kSumTP - 1) / kSumTP;
+    return mg.smem() <= budget && sg.smem() <= budget && g.N * g.C * strips < (1ll << 31) / 64 &&
+           g.N * g.C * strips * bands < (1ll << 31);
+}
+
+// The gather's target map from direct records (every word of it is written).
+template <typename I>
+void launch_pull_mark_t(const Geometry& g, const void* win, uint32_t* map, int border, cudaStream_t stream) {
+    const int H = static_cast<int>(g.H), W = static_cast<int>(g.W);
+    const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW);
+    const PullGeom geo(kH, kW, sizeof(I));
+    const int strips = ceil_div(W, kPullTQ);
+    const long long ctas = g.N * g.C * strips;
+    // enough CTAs for several waves; each segment re-reads 2aH rows, so keep them >= 4 bands
+    const long long want = std::clamp<long long>((2400 + ctas - 1) / ctas, 1, std::max(1, H / (4 * kPullTB)));
+    const int seg_h = static_cast<int>((H + want - 1) / want);
+    const int segs = ceil_div(H, seg_h);
+    const int rec_vec = (reinterpret_cast<uintptr_t>(win) & 15) == 0 && (W * sizeof(I)) % 16 == 0;
+    auto mark = pull_mark_kernel<I>;
+    set_smem(mark, geo.smem());
+    mark<<<grid_1d(ctas * segs), kPullThreads, geo.smem(), stream>>>(static_cast<const I*>(win), map, H, W, kH, kW,
+                                                                      border, strips, segs, seg_h, rec_vec);
+    SB_CUDA(cudaGetLastError());
+}
+
+// Forward; with a record buffer of a map format, the target map too (set by the separable sweep as it
+// writes the records, or built from the records afterwards).
 void launch_forward(int op, int dtype, int algo, const Geometry& g, const void* x, const void* w, void* y, void* win,
-                    int fmt, int border, cudaStream_t stream) {
+                    int fmt, int border, size_t budget, cudaStream_t stream) {
     dispatch_dtype(dtype, [&](auto t) {
         using T = decltype(t);
         dispatch_op(op, [&](auto o) {
             constexpr int OP = decltype(o)::value;
             if (win == nullptr) {
-                launch_forward_t<T, OP, uint8_t, true, false>(algo, g, x, w, y, nullptr, border, stream);
+                launch_forward_t<T, OP, uint8_t, true, false>(algo, g, x, w, y, nullptr, nullptr, border, stream);
                 return;
+            }
+            uint32_t* map = nullptr;
+            if (format_has_map(fmt)) {
+                map = reinterpret_cast<uint32_t*>(static_cast<char*>(win) + records_bytes(g, fmt));
+                SB_CUDA(cudaMemsetAsync(map, 0, pull_map_words(g.N * g.C, g.H, g.W) * 4, stream));
             }
             dispatch_index(fmt, [&](auto i) {
                 using I = decltype(i);
-                if (y != nullptr)
-                    launch_forward_t<T, OP, I, true, true>(algo, g, x, w, y, win, border, stream);
-                else
-                    launch_forward_t<T, OP, I, false, true>(algo, g, x, w, nullptr, win, border, stream);
+                const bool filled = y != nullptr
+                                        ? launch_forward_t<T, OP, I, true, true>(algo, g, x, w, y, win, map, border, stream)
+                                        : launch_forward_t<T, OP, I, false, true>(algo, g, x, w, nullptr, win, map,
+                                                                                  border, stream);
+                if (map && !filled && pull_applicable(g, border, sizeof(T), sizeof(I), budget))
+                    launch_pull_mark_t<I>(g, win, map, border, stream);
             });
         });
     });
 }
 
-// backward workspace layout: [winners][segrad partials][segrad global bins][target map], each 256-byte
-// aligned; the winners only when the backward computes them, the segrad parts only for grad_kernel
+// backward workspace layout: [winner records][target map][segrad partials][segrad global bins], each
+// 256-byte aligned; the records only when the backward computes them (the map then follows them, as in a
+// record buffer of a map format), the map only when the records come without one, the segrad parts
+// only for grad_kernel
 struct SegradPlan {
     int chunks = 0;
     int threads = 0;
@@ -429,24 +492,21 @@ SegradPlan segrad_plan(const Geometry& g) {
     p.bins_bytes = p.global_bins ? g.C * p.chunks * int64_t(p.threads) * bins * 8 : 0;
     return p;
 }
-int64_t align256(int64_t v) { return (v + 255) / 256 * 256; }
-
 int64_t segrad_workspace(const Geometry& g, bool need_kg) {
     if (!need_kg) return 0;
     const SegradPlan p = segrad_plan(g);
     return align256(p.partial_bytes) + align256(p.bins_bytes);
 }
-int64_t map_workspace(const Geometry& g) { return align256(pull_map_words(g.N * g.C, g.H, g.W) * 4); }
-
 int64_t backward_workspace(const Geometry& g, bool need_kg, int fmt, bool with_winners) {
     int64_t bytes = 0;
-    if (!with_winners) bytes += align256(g.numel() * format_bytes(fmt));
-    return bytes + segrad_workspace(g, need_kg) + map_workspace(g);
+    if (!with_winners) bytes += records_bytes(g, fmt);
+    if (!with_winners || !format_has_map(fmt)) bytes += map_workspace(g);
+    return bytes + segrad_workspace(g, need_kg);
 }
 
 template <typename T, typename I, bool SEP>
-void launch_gather_t(const Geometry& g, const void* go, const void* win, void* gi, uint32_t* map, int border,
-                     size_t budget, cudaStream_t stream) {
+void launch_gather_t(const Geometry& g, const void* go, const void* win, void* gi, uint32_t* map, bool map_ready,
+                     int border, size_t budget, cudaStream_t stream) {
     const int H = static_cast<int>(g.H), W = static_cast<int>(g.W);
     const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW);
     const int dtype = std::is_same<T, double>::value ? kF64 : kF32;
@@ -462,39 +522,22 @@ void launch_gather_t(const Geometry& g, const void* go, const void* win, void* g
         // mark-and-pull and raster-order stream gathers: every candidate must lie within a single border fold
         const bool single_fold = border != kReflect || (kH / 2 <= H - 1 && kH - 1 - kH / 2 <= H - 1 &&
                                                         kW / 2 <= W - 1 && kW - 1 - kW / 2 <= W - 1);
-        if (!SEP && single_fold && map != nullptr && pull_taps_fit(kH, kW, sizeof(I))) {
-            const PullGeom geo(kH, kW, sizeof(I));
-            const size_t mark_smem = geo.smem();
-            const int strips = ceil_div(W, kPullTQ);
-            const long long ctas = g.N * g.C * strips;
-            const SumGeom sgeo_check(kH, kW, sizeof(T), sizeof(I));
-            if (mark_smem <= budget && sgeo_check.smem() <= budget && ctas < (1ll << 31) / 64 &&
-                g.N * g.C * ceil_div(W, kPullTQ) * static_cast<long long>(ceil_div(H, kSumTP)) < (1ll << 31)) {
-                // enough CTAs for several waves; each segment re-reads 2aH rows, so keep them >= 4 bands
-                const long long want = std::clamp<long long>((2400 + ctas - 1) / ctas, 1, std::max(1, H / (4 * kPullTB)));
-                const int seg_h = static_cast<int>((H + want - 1) / want);
-                const int segs = ceil_div(H, seg_h);
-                auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
-                const int rec_vec = aligned(win) && (W * sizeof(I)) % 16 == 0;
-                const int out_vec = aligned(gi) && (W * sizeof(T)) % 16 == 0;
-                auto mark = pull_mark_kernel<T, I>;
-                set_smem(mark, mark_smem);
-                mark<<<grid_1d(ctas * segs), kPullThreads, mark_smem, stream>>>(
-                    static_cast<const I*>(win), static_cast<T*>(gi), map, H, W, kH, kW, border, strips, segs, seg_h,
-                    rec_vec, out_vec);
-                SB_CUDA(cudaGetLastError());
-                const SumGeom sgeo(kH, kW, sizeof(T), sizeof(I));
-                const int tiles_x = ceil_div(W, kPullTQ), tiles_y = ceil_div(H, kSumTP);
-                const int go_vec = aligned(go) && (W * sizeof(T)) % 16 == 0;
-                auto sum = pull_sum_kernel<T, I>;
-                set_smem(sum, sgeo.smem());
-                SB_CUDA(cudaFuncSetAttribute(sum, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-                sum<<<grid_1d(g.N * g.C * tiles_x * tiles_y), kSumThreads, sgeo.smem(), stream>>>(
-                    static_cast<const T*>(go), static_cast<const I*>(win), map, static_cast<T*>(gi), H, W, kH, kW,
-                    border, tiles_x, tiles_y, go_vec, rec_vec);
-                SB_CUDA(cudaGetLastError());
-                return;
-            }
+        if (!SEP && map != nullptr && pull_applicable(g, border, sizeof(T), sizeof(I), budget)) {
+            if (!map_ready) launch_pull_mark_t<I>(g, win, map, border, stream);
+            const SumGeom sgeo(kH, kW, sizeof(T), sizeof(I));
+            const int tiles_x = ceil_div(W, kPullTQ), tiles_y = ceil_div(H, kSumTP);
+            auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+            const int go_vec = aligned(go) && (W * sizeof(T)) % 16 == 0;
+            const int rec_vec = aligned(win) && (W * sizeof(I)) % 16 == 0;
+            const int out_vec = aligned(gi) && (W * sizeof(T)) % 16 == 0;
+            auto sum = pull_sum_kernel<T, I>;
+            set_smem(sum, sgeo.smem());
+            SB_CUDA(cudaFuncSetAttribute(sum, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+            sum<<<grid_1d(g.N * g.C * tiles_x * tiles_y), kSumThreads, sgeo.smem(), stream>>>(
+                static_cast<const T*>(go), static_cast<const I*>(win), map, static_cast<T*>(gi), H, W, kH, kW, border,
+                tiles_x, tiles_y, go_vec, rec_vec, out_vec);
+            SB_CUDA(cudaGetLastError());
+            return;
         }
         const StreamGeom geo(kH, kW, sizeof(I));
         const size_t stream_smem = geo.smem(sizeof(typename GradAcc<T>::type), sizeof(I));
@@ -554,19 +597,19 @@ void launch_segrad_t(int op, const Geometry& g, const void* go, const void* win,
     SB_CUDA(cudaGetLastError());
 }
 
+// `map`: the target map (ready: filled from these records), `ws`: the segrad workspace.
 void launch_backward_from_winners(int op, int dtype, const Geometry& g, const void* go, const void* win, int fmt,
-                                  void* gi, void* gk, bool need_kg, void* ws, int border, size_t budget,
-                                  cudaStream_t stream) {
+                                  void* gi, void* gk, bool need_kg, uint32_t* map, bool map_ready, void* ws,
+                                  int border, size_t budget, cudaStream_t stream) {
     const bool sep = format_is_separable(fmt);
-    uint32_t* map = reinterpret_cast<uint32_t*>(static_cast<char*>(ws) + segrad_workspace(g, need_kg));
     dispatch_dtype(dtype, [&](auto t) {
         using T = decltype(t);
         dispatch_index(fmt, [&](auto i) {
             using I = decltype(i);
             if (sep)
-                launch_gather_t<T, I, true>(g, go, win, gi, map, border, budget, stream);
+                launch_gather_t<T, I, true>(g, go, win, gi, map, map_ready, border, budget, stream);
             else
-                launch_gather_t<T, I, false>(g, go, win, gi, map, border, budget, stream);
+                launch_gather_t<T, I, false>(g, go, win, gi, map, map_ready, border, budget, stream);
             if (need_kg) {
                 if (sep)
                     launch_segrad_t<T, I, true>(op, g, go, win, gk, ws, border, stream);
@@ -601,12 +644,13 @@ int forward_impl(int op, const void* input, const int64_t* in_sizes, int64_t in_
         const Problem p{g.kH, g.kW, is_flat, dtype, info.smem_optin, separable_min_k(device, dtype, false)};
         const int resolved = resolve_algorithm(requested, p, name);
         if (winners) {
+            // the plan's format, or the same records without the map
             const int want = winners_format_for(resolved, g.kH, g.kW);
-            SB_CHECK(winners_format == want, name, ": winner format ", winners_format,
-                     " does not match the resolved algorithm (expected ", want, ")");
+            SB_CHECK(winners_format == want || winners_format == base_format(want), name, ": winner format ",
+                     winners_format, " does not match the resolved algorithm (expected ", want, ")");
         }
         launch_forward(op, dtype, resolved, g, input, kernel, output, winners, winners_format, static_cast<int>(border),
-                       stream);
+                       info.smem_optin, stream);
     });
 }
 
@@ -640,10 +684,12 @@ int backward_impl(int op, const void* grad_output, const int64_t* go_sizes, int6
             throw Failure{SERRON_ERR_WORKSPACE, concat(name, ": workspace of ", workspace_bytes, " bytes, ", need, " needed")};
         char* ws = static_cast<char*>(workspace);
         void* win = ws;
-        launch_forward(op, dtype, resolved, g, input, kernel, nullptr, win, fmt, static_cast<int>(border), stream);
-        launch_backward_from_winners(op, dtype, g, grad_output, win, fmt, grad_input, grad_kernel, need_kg != 0,
-                                     ws + align256(g.numel() * format_bytes(fmt)), static_cast<int>(border),
-                                     info.smem_optin, stream);
+        uint32_t* map = reinterpret_cast<uint32_t*>(ws + records_bytes(g, fmt));
+        launch_forward(op, dtype, resolved, g, input, kernel, nullptr, win, fmt, static_cast<int>(border),
+                       info.smem_optin, stream);
+        launch_backward_from_winners(op, dtype, g, grad_output, win, fmt, grad_input, grad_kernel, need_kg != 0, map,
+                                     format_has_map(fmt), ws + records_bytes(g, fmt) + map_workspace(g),
+                                     static_cast<int>(border), info.smem_optin, stream);
     });
 }
 
@@ -793,6 +839,27 @@ int serron_forward(int32_t op, const void* input, const int64_t* input_sizes, in
                         output, winners, winners_format, device, stream);
 }
 
+int64_t serron_winners_bytes(const int64_t* sizes, int64_t dim, int32_t winners_format) {
+    int64_t out = -1;
+    const int rc = guarded([&] {
+        const char* name = "serron::winners_bytes";
+        SB_CHECK(dim == 4 && sizes != nullptr, name, ": input must be 4-D (N, C, H, W), got ", dim, "-D");
+        const int base = base_format(winners_format);
+        SB_CHECK(base >= SERRON_WINNERS_DIRECT_U8 && base <= SERRON_WINNERS_SEPARABLE_U32 &&
+                     (winners_format & ~(SERRON_WINNERS_MAP | 0xf)) == 0 &&
+                     !(format_has_map(winners_format) && format_is_separable(winners_format)),
+                 name, ": invalid winner format ", winners_format);
+        Geometry g;
+        g.N = sizes[0];
+        g.C = sizes[1];
+        g.H = sizes[2];
+        g.W = sizes[3];
+        SB_CHECK(g.N >= 0 && g.C >= 0 && g.H >= 0 && g.W >= 0, name, ": input sizes must be non-negative");
+        out = winners_buffer_bytes(g, winners_format);
+    });
+    return rc == SERRON_OK ? out : -1;
+}
+
 int serron_plan(const int64_t* input_sizes, int64_t input_dim, const void* kernel, const int64_t* kernel_sizes,
                 int64_t kernel_dim, int32_t dtype, int32_t flat, int64_t algo, int32_t backward, int32_t device,
                 void* stream, serron_plan_t* plan) {
@@ -847,10 +914,13 @@ int serron_backward_from_winners(int32_t op, const void* grad_output, const int6
         SB_CHECK(op == kErode || op == kDilate, "serron: invalid op ", op);
         const Geometry g = parse_geometry(name, sizes, dim, kernel_sizes, kernel_dim);
         check_common(name, dtype, border);
-        SB_CHECK(winners_format >= SERRON_WINNERS_DIRECT_U8 && winners_format <= SERRON_WINNERS_SEPARABLE_U32, name,
-                 ": invalid winner format ", winners_format);
-        const int want = format_is_separable(winners_format) ? separable_format(g.kH, g.kW) : direct_format(g.kH, g.kW);
-        SB_CHECK(winners_format == want, name, ": winner format ", winners_format, " does not fit a ", g.kH, "x", g.kW,
+        const int base = base_format(winners_format);
+        SB_CHECK(base >= SERRON_WINNERS_DIRECT_U8 && base <= SERRON_WINNERS_SEPARABLE_U32 &&
+                     (winners_format & ~(SERRON_WINNERS_MAP | 0xf)) == 0 &&
+                     !(format_has_map(winners_format) && format_is_separable(winners_format)),
+                 name, ": invalid winner format ", winners_format);
+        const int want = format_is_separable(base) ? separable_format(g.kH, g.kW) : direct_format(g.kH, g.kW);
+        SB_CHECK(base == want, name, ": winner format ", winners_format, " does not fit a ", g.kH, "x", g.kW,
                  " window");
         DeviceScope scope(device);
         cudaStream_t s = static_cast<cudaStream_t>(stream);
@@ -863,8 +933,14 @@ int serron_backward_from_winners(int32_t op, const void* grad_output, const int6
             throw Failure{SERRON_ERR_WORKSPACE, concat(name, ": workspace of ", workspace_bytes, " bytes, ", need, " needed")};
         SB_CHECK(grad_output && winners && grad_input && grad_kernel, name, ": null tensor pointer");
         const DeviceInfo info = device_info(device);
+        const bool has_map = format_has_map(winners_format);
+        char* ws = static_cast<char*>(workspace);
+        uint32_t* map = has_map ? reinterpret_cast<uint32_t*>(static_cast<char*>(const_cast<void*>(winners)) +
+                                                              records_bytes(g, winners_format))
+                                : reinterpret_cast<uint32_t*>(ws);
         launch_backward_from_winners(op, dtype, g, grad_output, winners, winners_format, grad_input, grad_kernel,
-                                     need_kernel_grad != 0, workspace, static_cast<int>(border), info.smem_optin, s);
+                                     need_kernel_grad != 0, map, has_map, has_map ? ws : ws + map_workspace(g),
+                                     static_cast<int>(border), info.smem_optin, s);
     });
 }
 

@@ -10,16 +10,18 @@
 //                     them (the strip widened by aW columns) through a shared-memory ring, one band of
 //                     kPullTB rows ahead with cp.async.  Every record is decoded into the pixel it
 //                     selects (borders folded) and that pixel is marked.  Each finished band leaves
-//                     as one bit per pixel in the target map, and as zeros in grad_input.
-//   pull_sum_kernel   computes the winners' sums.  A CTA owns a kSumTP x kPullTQ tile, reads its map
-//                     words (and stops there when they are empty), stages grad_output and the records
+//                     as one bit per pixel in the target map.  (The separable sweep forward sets the
+//                     map itself while it writes the records; then this launch is skipped.)
+//   pull_sum_kernel   computes grad_input.  A CTA owns a kSumTP x kPullTQ tile, reads its map words
+//                     (and writes zeros when they are empty), stages grad_output and the records
 //                     of the tile grown by the box halo in shared memory with cp.async, lists the set
 //                     bits, and one thread per winner p walks the (2aH+1) x (2aW+1) box of outputs around
 //                     p in raster order, adding grad_output of each output that selects p: exactly the
 //                     reference's sequence of additions for p, with no atomics and no ordering between
 //                     threads.  Inside the image an odd window's record IS the box tap of its winner,
 //                     (dr + aH) * kW + (dc + aW), so for boxes up to 15 x 15 the test runs on four
-//                     one-byte records at a time against constants, with the box unrolled.
+//                     one-byte records at a time against constants, with the box unrolled.  The tile
+//                     leaves whole (zeros where nothing won), in 16-byte stores.
 //
 // Every candidate must lie within a single border fold; the host sends windows wider than the image
 // under REFLECT elsewhere.
@@ -85,11 +87,10 @@ __host__ __device__ inline long long pull_map_words(long long planes, long long 
     return planes * H * ((W + 31) / 32);
 }
 
-template <typename T, typename I>
-__global__ void __launch_bounds__(kPullThreads, 4) pull_mark_kernel(const I* __restrict__ win, T* __restrict__ gi,
-                                                                    uint32_t* __restrict__ map, int H, int W, int kH,
-                                                                    int kW, int border, int strips, int segs,
-                                                                    int seg_h, int rec_vec, int out_vec) {
+template <typename I>
+__global__ void __launch_bounds__(kPullThreads, 4) pull_mark_kernel(const I* __restrict__ win, uint32_t* __restrict__ map,
+                                                                    int H, int W, int kH, int kW, int border,
+                                                                    int strips, int segs, int seg_h, int rec_vec) {
     constexpr int TQ = kPullTQ, TB = kPullTB, NT = kPullThreads;
     constexpr uint32_t kNone = IndexTraits<I>::none;
     const PullGeom geo(kH, kW, sizeof(I));
@@ -107,7 +108,6 @@ __global__ void __launch_bounds__(kPullThreads, 4) pull_mark_kernel(const I* __r
     const int c0 = strip * TQ;
     const int ph0 = seg * seg_h, ph1 = min(H, ph0 + seg_h);
     const I* wp = win + plane * H * W;
-    T* gip = gi + plane * H * W;
     const int WW = (W + 31) / 32;
     uint32_t* mapp = map + plane * H * WW;
     const int tid = threadIdx.x;
@@ -219,7 +219,6 @@ __global__ void __launch_bounds__(kPullThreads, 4) pull_mark_kernel(const I* __r
         __syncthreads();
 
         // the band leaves as target-map words (a thread packs the 32 mark bytes of a word, each 0 or 1)
-        // and as zeros in grad_input
         for (int i = tid; i < nb * (TQ / 32); i += NT) {
             const int r = i / (TQ / 32), k = i - r * (TQ / 32);
             int ms = mbase + r;
@@ -232,20 +231,6 @@ __global__ void __launch_bounds__(kPullThreads, 4) pull_mark_kernel(const I* __r
 #pragma unroll
             for (int e = 0; e < 8; ++e) bits |= ((q[e] | (q[e] >> 7) | (q[e] >> 14) | (q[e] >> 21)) & 0xfu) << (4 * e);
             if (c0 / 32 + k < WW) mapp[static_cast<long long>(R + r) * WW + c0 / 32 + k] = bits;
-        }
-        {
-            const int ov = 16 / int(sizeof(T));
-            const uint4 zero = make_uint4(0, 0, 0, 0);
-            for (int i = tid; i < nb * (TQ / ov); i += NT) {
-                const int r = i / (TQ / ov), c = c0 + (i - r * (TQ / ov)) * ov;
-                if (c >= W) continue;
-                T* dst = gip + static_cast<long long>(R + r) * W + c;
-                if (out_vec && c + ov <= W) {
-                    *reinterpret_cast<uint4*>(dst) = zero;
-                } else {
-                    for (int e = 0; e < ov && c + e < W; ++e) dst[e] = Storage<T>::store(0.0f);
-                }
-            }
         }
         mbase += TB;
         if (mbase >= MR) mbase -= MR;
@@ -267,7 +252,7 @@ constexpr int kSumThreads = 128;
 // row, with a few bytes of slack behind the record row for word-wise reads.
 struct SumGeom {
     int aH, aW, hr, hq, gv, goff, gq, rv, roff, rq;
-    size_t go_b, rec_b, list_b;
+    size_t go_b, rec_b, list_b, res_b;
     __host__ __device__ SumGeom(int kH, int kW, int elem, int idx)
         : aH(kH / 2), aW(kW / 2), hr(kSumTP + 2 * (kH / 2)), hq(kPullTQ + 2 * (kW / 2)) {
         gv = 16 / elem;
@@ -279,8 +264,9 @@ struct SumGeom {
         go_b = (size_t(hr) * gq * elem + 15) / 16 * 16;
         rec_b = (size_t(hr) * rq * idx + 15) / 16 * 16;
         list_b = size_t(kSumTP) * kPullTQ * 2;
+        res_b = size_t(kSumTP) * kPullTQ * elem;
     }
-    __host__ __device__ size_t smem() const { return go_b + rec_b + list_b + 16; }
+    __host__ __device__ size_t smem() const { return go_b + rec_b + list_b + res_b + 16; }
 };
 
 // Sum for one pixel over its KB x KB box (KB = 2a + 1) of one-byte box taps staged in shared memory.
@@ -354,7 +340,7 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
                                                                const uint32_t* __restrict__ map,
                                                                T* __restrict__ gi, int H, int W, int kH, int kW,
                                                                int border, int tiles_x, int tiles_y, int go_vec,
-                                                               int rec_vec) {
+                                                               int rec_vec, int out_vec) {
     using G = typename GradAcc<T>::type;
     constexpr int TP = kSumTP, TQ = kPullTQ, NT = kSumThreads, NWORDS = TP * TQ / 32;
     constexpr uint32_t kNone = IndexTraits<I>::none;
@@ -366,7 +352,8 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
     T* goS = reinterpret_cast<T*>(smem_raw);                                          // [hr][gq]
     I* recS = reinterpret_cast<I*>(smem_raw + geo.go_b);                              // [hr][rq]
     uint16_t* listS = reinterpret_cast<uint16_t*>(smem_raw + geo.go_b + geo.rec_b);   // [TP * TQ]
-    int* countS = reinterpret_cast<int*>(smem_raw + geo.go_b + geo.rec_b + geo.list_b);
+    T* resS = reinterpret_cast<T*>(smem_raw + geo.go_b + geo.rec_b + geo.list_b);     // [TP][TQ]
+    int* countS = reinterpret_cast<int*>(smem_raw + geo.go_b + geo.rec_b + geo.list_b + geo.res_b);
 
     const long long b = blockIdx.x;
     const int tx = static_cast<int>(b % tiles_x);
@@ -384,7 +371,28 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
         wcol = c0 / 32 + tid % (TQ / 32);
         if (wrow < H && wcol < WW) bits = map[(plane * H + wrow) * WW + wcol];
     }
-    if (!__syncthreads_or(bits != 0u)) return;  // no winner in the tile: grad_input stays zero
+    // the tile leaves in 16-byte stores, from the result tile or (no winner in it) as zeros
+    T* gip = gi + plane * H * W;
+    auto write_tile = [&](bool zeros) {
+        constexpr int OV = 16 / int(sizeof(T));
+        const uint4 zero4 = make_uint4(0, 0, 0, 0);
+        for (int i = tid; i < TP * TQ / OV; i += NT) {
+            const int pr = i / (TQ / OV), pc = (i - pr * (TQ / OV)) * OV;
+            const int r = r0 + pr, c = c0 + pc;
+            if (r >= H || c >= W) continue;
+            T* dst = gip + static_cast<long long>(r) * W + c;
+            if (out_vec && c + OV <= W) {
+                *reinterpret_cast<uint4*>(dst) = zeros ? zero4 : reinterpret_cast<const uint4*>(resS)[i];
+            } else {
+                for (int e = 0; e < OV && c + e < W; ++e) dst[e] = zeros ? Storage<T>::store(0.0f) : resS[pr * TQ + pc + e];
+            }
+        }
+    };
+    if (!__syncthreads_or(bits != 0u)) {  // no winner in the tile
+        write_tile(true);
+        return;
+    }
+    for (int i = tid; i < int(geo.res_b / 16); i += NT) reinterpret_cast<uint4*>(resS)[i] = make_uint4(0, 0, 0, 0);
 
     // stage grad_output and records of output rows [r0 - aH, r0 + TP + aH) inside the image
     const T* gop = go + plane * H * W;
@@ -465,7 +473,6 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
     // one thread per winner: the outputs of its box, in raster order
     const int n = *countS;
     const bool box_fixed = sizeof(I) == 1 && kH == kW && (kW & 1) && kW >= 3 && kW <= 15;
-    T* gip = gi + plane * H * W;
     for (int k = tid; k < n; k += NT) {
         const int p = listS[k];
         const int pr = p / TQ, pc = p - pr * TQ;  // box rows pr .. pr + 2aH, columns pc .. pc + 2aW (staged)
@@ -494,8 +501,10 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
                         acc = GradAcc<T>::add(acc, static_cast<G>(Storage<T>::load(grow[j])));
             }
         }
-        gip[static_cast<long long>(x) * W + y] = Storage<T>::store(static_cast<typename Storage<T>::acc>(acc));
+        resS[p] = Storage<T>::store(static_cast<typename Storage<T>::acc>(acc));
     }
+    __syncthreads();
+    write_tile(false);
 }
 
 // The box taps of a (kH, kW) window, and the "none" record, fit in a record of `idx` bytes.

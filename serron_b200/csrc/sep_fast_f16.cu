@@ -2,6 +2,6 @@
 #include "sep_fast_launch.cuh"
 
 namespace serron {
-template int sep_fast_fwd_t<__half>(int, int, bool, bool, const void*, void*, void*, long long, int, int, int,
-                                  cudaStream_t);
+template int sep_fast_fwd_t<__half>(int, int, bool, bool, const void*, void*, void*, uint32_t*, long long, int, int,
+                                    int, cudaStream_t);
 }  // namespace serron

@@ -33,8 +33,8 @@ inline void sweep_segments(long long planes, int strips, int H, int step, int& s
 }
 
 template <typename T, int OP, int K, bool V, bool X>
-int sep_fast_fwd_launch(const void* x, void* y, void* win, long long planes, int H, int W, int border,
-                        cudaStream_t stream) {
+int sep_fast_fwd_launch(const void* x, void* y, void* win, uint32_t* map, long long planes, int H, int W,
+                        int border, cudaStream_t stream) {
     using G = SweepGeom<K, sizeof(T)>;
     using I = FastIndex<K>;
     const int strips = (W + kSweepTW - 1) / kSweepTW;
@@ -46,27 +46,29 @@ int sep_fast_fwd_launch(const void* x, void* y, void* win, long long planes, int
     if (err != cudaSuccess) return static_cast<int>(err);
     const long long blocks = planes * strips * segs;
     kernel<<<static_cast<unsigned>(blocks), kSweepThreads, smem, stream>>>(
-        static_cast<const T*>(x), static_cast<T*>(y), static_cast<I*>(win), H, W, border, strips, segs, seg_h);
+        static_cast<const T*>(x), static_cast<T*>(y), static_cast<I*>(win), map, H, W, border, strips, segs, seg_h);
     return static_cast<int>(cudaGetLastError());
 }
 
 template <typename T, int OP, int K>
-int sep_fast_fwd_k(bool with_value, bool with_index, const void* x, void* y, void* win, long long planes, int H,
-                   int W, int border, cudaStream_t stream) {
-    if (with_value && with_index) return sep_fast_fwd_launch<T, OP, K, true, true>(x, y, win, planes, H, W, border, stream);
-    if (with_index) return sep_fast_fwd_launch<T, OP, K, false, true>(x, y, win, planes, H, W, border, stream);
-    return sep_fast_fwd_launch<T, OP, K, true, false>(x, y, win, planes, H, W, border, stream);
+int sep_fast_fwd_k(bool with_value, bool with_index, const void* x, void* y, void* win, uint32_t* map, long long planes,
+                   int H, int W, int border, cudaStream_t stream) {
+    if (with_value && with_index)
+        return sep_fast_fwd_launch<T, OP, K, true, true>(x, y, win, map, planes, H, W, border, stream);
+    if (with_index) return sep_fast_fwd_launch<T, OP, K, false, true>(x, y, win, map, planes, H, W, border, stream);
+    return sep_fast_fwd_launch<T, OP, K, true, false>(x, y, win, nullptr, planes, H, W, border, stream);
 }
 
-// Returns 0 on success, a cudaError_t code on a launch failure, or -1 when K has no fast path.
+// Returns 0 on success, a cudaError_t code on a launch failure, or -1 when K has no fast path.  With
+// `map` (zeroed by the caller) the winners are also set in the gather's target map.
 template <typename T>
-int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win,
+int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win, uint32_t* map,
                    long long planes, int H, int W, int border, cudaStream_t stream) {
 #define SERRON_SEP_FAST_FWD_CASE(k)                                                                         \
     case k:                                                                                                 \
-        return op == kErode ? sep_fast_fwd_k<T, kErode, k>(with_value, with_index, x, y, win, planes, H, W,   \
-                                                           border, stream)                                  \
-                            : sep_fast_fwd_k<T, kDilate, k>(with_value, with_index, x, y, win, planes, H, W,  \
+        return op == kErode ? sep_fast_fwd_k<T, kErode, k>(with_value, with_index, x, y, win, map, planes, H, W, \
+                                                           border, stream)                                     \
+                            : sep_fast_fwd_k<T, kDilate, k>(with_value, with_index, x, y, win, map, planes, H, W,\
                                                             border, stream);
     switch (K) {
         SERRON_SEP_FAST_KS(SERRON_SEP_FAST_FWD_CASE)

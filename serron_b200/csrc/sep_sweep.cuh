@@ -83,10 +83,15 @@ __device__ __forceinline__ float load_clean(T v, float neutral) {
     return f != f ? neutral : f;  // NaN never wins: staged as the neutral element
 }
 
+// With `map` (records only), every winner is also set in the target map of the gather (one bit per
+// pixel, rows of ceil(W / 32) words, zero on entry): an output flags the row result its winner lies in
+// (bit 7 of that result's dj byte), and after the step each flagged result ORs its pixel into the map.
 template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX, int K>
 __global__ void __launch_bounds__(kSweepThreads) sep_sweep_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
-                                                                      I* __restrict__ win, int H, int W, int border,
-                                                                      int strips, int segs, int seg_h) {
+                                                                      I* __restrict__ win, uint32_t* __restrict__ map,
+                                                                      int H, int W, int border, int strips, int segs,
+                                                                      int seg_h) {
+    static_assert(K <= 128, "dj and its flag share a byte");
     using G = SweepGeom<K, sizeof(T)>;
     constexpr int a = G::a, TH = G::TH, Cc = G::Cc, XS = G::XS, RS = G::RS;
     constexpr bool ASYNC = sizeof(T) == 4;
@@ -109,6 +114,8 @@ __global__ void __launch_bounds__(kSweepThreads) sep_sweep_fwd_kernel(const T* _
     const bool cols_inside = ow0 - a >= 0 && ow0 - a + Cc <= W;
 
     const int warp = tid >> 5, lane = tid & 31;
+    const bool marking = WITH_INDEX && map != nullptr;
+    const int WW = (W + 31) / 32;
 
     // rows [r0, r0 + nrows) of the image (unresolved) -> buffer rows [0, nrows); one warp per row
     auto stage = [&](T* buf, int r0, int nrows) {
@@ -196,11 +203,13 @@ __global__ void __launch_bounds__(kSweepThreads) sep_sweep_fwd_kernel(const T* _
 
         // column pass: output row s0 + i uses row results [i, i + K - 1]
         const int rows_left = oh_end - s0;  // >= TH except in a segment's last step
+        // (the task count is a multiple of 32, so every warp runs whole: lanes past the image edge stay in
+        // the loop with nothing to write, and the winner de-duplication below can shuffle across the warp)
         for (int task = tid; task < G::NCC * kSweepTW; task += kSweepThreads) {
             const int c = task / kSweepTW, j = task - c * kSweepTW;
             const int base = c * K;
             const int ow = ow0 + j;
-            if (ow >= W) continue;
+            const bool col_ok = ow < W;
             float v[2 * K - 1];
 #pragma unroll
             for (int m = 0; m < 2 * K - 1; ++m) v[m] = rv[(base + m) * RS + j];
@@ -208,21 +217,47 @@ __global__ void __launch_bounds__(kSweepThreads) sep_sweep_fwd_kernel(const T* _
             const int o0 = (s0 + base) * W + ow;
             T* yp = y + plane * H * W;
             I* wp = win + plane * H * W;
-            const uint8_t* dj_col = rdj + base * RS + j;
+            uint8_t* dj_col = rdj + base * RS + j;
             sweep_run<K, OP, WITH_INDEX>(v, [&](int m, float val, int off) {
-                if (base + m < rows_left) {
-                    const int o = o0 + m * W;
-                    if (WITH_VALUE) yp[o] = Storage<T>::store(val);
-                    if (WITH_INDEX) {
-                        // winning row base + m + off, and the column its own row pass chose
-                        const uint32_t t = val == neutral ? IndexTraits<I>::none
-                                                          : static_cast<uint32_t>(off) * K + dj_col[(m + off) * RS];
-                        wp[o] = static_cast<I>(t);
-                    }
+                const bool out_ok = col_ok && base + m < rows_left;
+                const int o = o0 + m * W;
+                if (WITH_VALUE && out_ok) yp[o] = Storage<T>::store(val);
+                if (WITH_INDEX && out_ok) {
+                    // winning row base + m + off, and the column its own row pass chose (bit 7: flagged)
+                    const uint32_t djb = dj_col[(m + off) * RS];
+                    const uint32_t t =
+                        val == neutral ? IndexTraits<I>::none : static_cast<uint32_t>(off * K) + (djb & 0x7fu);
+                    wp[o] = static_cast<I>(t);
+                    // every writer of the flag writes the same byte
+                    if (marking && val != neutral) dj_col[(m + off) * RS] = static_cast<uint8_t>(djb | 0x80u);
                 }
             });
         }
         __syncthreads();
+        // flagged row results give the step's winners (row s0 - a + i, column ow0 + j - a + dj, border
+        // folded) to the target map; a lane skips the OR when its left neighbour, which usually has the same
+        // winner, does it.  Flags are cleared for the carry.  RR * 64 is a multiple of 32: warps run whole.
+        if (marking) {
+            for (int c = tid; c < G::RR * kSweepTW; c += kSweepThreads) {
+                const int i = c / kSweepTW, j = c - i * kSweepTW;
+                uint8_t* cell = rdj + i * RS + j;
+                const uint32_t d = *cell;
+                int wx = -1, wy = 0;
+                if (d & 0x80u) {
+                    *cell = static_cast<uint8_t>(d & 0x7fu);
+                    wx = s0 - a + i;
+                    wy = ow0 + j - a + static_cast<int>(d & 0x7fu);
+                    if (!((static_cast<unsigned>(wx) < static_cast<unsigned>(H) || resolve(wx, H, border)) &&
+                          (static_cast<unsigned>(wy) < static_cast<unsigned>(W) || resolve(wy, W, border))))
+                        wx = -1;
+                }
+                const int key = wx < 0 ? -1 : wx * W + wy;  // < H * W < 2^31
+                const int left = __shfl_up_sync(0xffffffffu, key, 1);
+                if (key >= 0 && (lane == 0 || left != key))
+                    atomicOr(&map[(plane * H + wx) * WW + (wy >> 5)], 1u << (wy & 31));
+            }
+            __syncthreads();
+        }
         // carry the last K-1 row results to the top
         for (int i = tid; i < (K - 1) * RS; i += kSweepThreads) {
             rv[i] = rv[TH * RS + i];
