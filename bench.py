@@ -37,14 +37,14 @@ METRIC = "output Gpix/s erode+dilate fwd+bwd per GPU at 1/2/4/8 B200; % of HBM/m
 WORKLOAD = "flat separable: dilation+erosion of x(32,64,512,512) fp32 uniform[0,1), square(15), REFLECT, fwd+bwd"
 PRIMS = 2  # primitive calls per step
 # algorithmic HBM bytes per output pixel of each timed stage (fp32 value 4 B, winner record 1 B):
-# "forward" is one launch of the separable sweep forward, "gather" the backward's two launches (target
-# map, then the winners' sums)
+# "forward" is one launch of the separable sweep forward (records and target map included), "gather"
+# the backward's launch of the winners' sums
 FWD_BYTES_PER_PX = 4 + 4 + 1  # read x, write y, write winners
 BWD_BYTES_PER_PX = 4 + 1 + 4  # read grad_output, read winners, write grad_input
 # per-call DRAM traffic of each stage at the full workload: dram__bytes_read + dram__bytes_write of a
 # 1/8-size capture (profiles/gather_pull_and_sweep_fwd_batch4.md), times 8
 NCU_TRAFFIC_BYTES = {"forward": 4.50e9, "gather": 5.49e9}
-LAUNCHES_PER_STEP = 2 * (1 + 2)  # per op: the forward, then the gather's mark and sum kernels
+LAUNCHES_PER_STEP = 2 * (1 + 1)  # per op: the forward, then the gather's sum kernel
 CPU_SAMPLE = (1, 4, 512, 512)  # slice of the workload the CPU baseline times (scaled linearly in pixels)
 
 
@@ -240,21 +240,55 @@ def run_ours(args) -> None:
     value = px * PRIMS * world / (ms_per_step * 1e-3) / 1e9
 
     # end to end through the public API with host buffers: H2D of the step's inputs from pinned memory,
-    # both ops forward + backward, D2H of both outputs and both input gradients
+    # both ops forward + backward, D2H of both outputs and both input gradients.  The batch goes through
+    # in chunks on three streams (copies in, compute, copies out) so that both copy directions overlap
+    # the compute and each other, as a user streaming host data through the API would run it.
     x_host = x.detach().cpu().pin_memory()
     go_host = go.cpu().pin_memory()
     outs = [torch.empty(shape, dtype=torch.float32).pin_memory() for _ in range(4)]
+    nch = min(8, shape[0])
+    bounds = [(i * shape[0] // nch, (i + 1) * shape[0] // nch) for i in range(nch)]
+    cshape = (max(e - b for b, e in bounds),) + shape[1:]
+    slots = [{"x": torch.empty(cshape, device=dev), "go": torch.empty(cshape, device=dev),
+              "out": [torch.empty(cshape, device=dev) for _ in range(4)]} for _ in range(2)]
+    s_in, s_cmp, s_out = (torch.cuda.Stream(dev) for _ in range(3))
 
     def e2e_step() -> None:
-        xd = x_host.to(dev, non_blocking=True).requires_grad_(True)
-        god = go_host.to(dev, non_blocking=True)
-        j = 0
-        for fn in (serron.dilation, serron.erosion):
-            y = fn(xd, k, border=border)
-            (gx,) = torch.autograd.grad(y, xd, god)
-            outs[j].copy_(y.detach(), non_blocking=True)
-            outs[j + 1].copy_(gx, non_blocking=True)
-            j += 2
+        ev_in = [torch.cuda.Event() for _ in bounds]
+        ev_cmp = [torch.cuda.Event() for _ in bounds]
+        ev_out = [torch.cuda.Event() for _ in bounds]
+        main = torch.cuda.current_stream(dev)
+        for st in (s_in, s_cmp, s_out):
+            st.wait_stream(main)
+        for i, (b0, b1) in enumerate(bounds):
+            sl, n = slots[i % 2], b1 - b0
+            with torch.cuda.stream(s_in):
+                if i >= 2:
+                    s_in.wait_event(ev_cmp[i - 2])  # the slot's inputs are consumed
+                sl["x"][:n].copy_(x_host[b0:b1], non_blocking=True)
+                sl["go"][:n].copy_(go_host[b0:b1], non_blocking=True)
+                ev_in[i].record(s_in)
+            with torch.cuda.stream(s_cmp):
+                s_cmp.wait_event(ev_in[i])
+                if i >= 2:
+                    s_cmp.wait_event(ev_out[i - 2])  # the slot's results are read back
+                xd = sl["x"][:n].detach().requires_grad_(True)
+                god = sl["go"][:n]
+                j = 0
+                for fn in (serron.dilation, serron.erosion):
+                    y = fn(xd, k, border=border)
+                    (gx,) = torch.autograd.grad(y, xd, god)
+                    sl["out"][j][:n].copy_(y.detach())
+                    sl["out"][j + 1][:n].copy_(gx)
+                    j += 2
+                ev_cmp[i].record(s_cmp)
+            with torch.cuda.stream(s_out):
+                s_out.wait_event(ev_cmp[i])
+                for j in range(4):
+                    outs[j][b0:b1].copy_(sl["out"][j][:n], non_blocking=True)
+                ev_out[i].record(s_out)
+        for st in (s_in, s_cmp, s_out):
+            main.wait_stream(st)
 
     e2e_steps = max(1, min(args.steps, 3))
     e2e_step()

@@ -87,7 +87,7 @@ __device__ __forceinline__ float load_clean(T v, float neutral) {
 // pixel, rows of ceil(W / 32) words, zero on entry): an output flags the row result its winner lies in
 // (bit 7 of that result's dj byte), and after the step each flagged result ORs its pixel into the map.
 template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX, int K>
-__global__ void __launch_bounds__(kSweepThreads) sep_sweep_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
+__global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                                       I* __restrict__ win, uint32_t* __restrict__ map,
                                                                       int H, int W, int border, int strips, int segs,
                                                                       int seg_h) {
