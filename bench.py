@@ -43,7 +43,7 @@ FWD_BYTES_PER_PX = 4 + 4 + 1  # read x, write y, write winners
 BWD_BYTES_PER_PX = 4 + 1 + 4  # read grad_output, read winners, write grad_input
 # per-call DRAM traffic of each stage at the full workload: dram__bytes_read + dram__bytes_write of a
 # 1/8-size capture (profiles/gather_pull_and_sweep_fwd_batch4.md), times 8
-NCU_TRAFFIC_BYTES = {"forward": 4.50e9, "gather": 5.49e9}
+NCU_TRAFFIC_BYTES = {"forward": 4.61e9, "gather": 4.63e9}
 LAUNCHES_PER_STEP = 2 * (1 + 1)  # per op: the forward, then the gather's sum kernel
 CPU_SAMPLE = (1, 4, 512, 512)  # slice of the workload the CPU baseline times (scaled linearly in pixels)
 
