@@ -45,7 +45,8 @@ BWD_BYTES_PER_PX = 4 + 1 + 4  # read grad_output, read winners, write grad_input
 # 1/8-size capture (profiles/gather_pull_and_sweep_fwd_batch4.md), times 8
 NCU_TRAFFIC_BYTES = {"forward": 4.61e9, "gather": 4.63e9}
 LAUNCHES_PER_STEP = 2 * (1 + 1)  # per op: the forward, then the gather's sum kernel
-CPU_SAMPLE = (1, 4, 512, 512)  # slice of the workload the CPU baseline times (scaled linearly in pixels)
+CPU_SAMPLE = (1, 64, 512, 512)  # one image of the batch: the slice the CPU baseline times (scaled by pixels)
+CPU_MIN_SECONDS = 10.0  # the baseline in our arm's line times at least this much CPU work
 
 
 def _peaks() -> tuple[float, str]:
@@ -120,8 +121,9 @@ def _dist() -> tuple[int, int, int]:
     return world, rank, local
 
 
-def _cpu_baseline(steps: int) -> dict:
-    """The reference's CPU path on a slice, all host threads; Gpix/s scaled by pixels."""
+def _cpu_baseline(steps: int | None = None, warmup: int = 1) -> dict:
+    """The reference's CPU path on a slice, all host threads; Gpix/s scaled by pixels.  With `steps`
+    None it times whole steps until CPU_MIN_SECONDS have passed (at least 3)."""
     import oracle
 
     torch.set_num_threads(os.cpu_count() or 1)
@@ -142,15 +144,22 @@ def _cpu_baseline(steps: int) -> dict:
                 oracle.forward(op, x, w, 0, separable=True)
                 oracle.backward(op, go, x, w, 0, separable=True, need_kernel_grad=False)
 
-    step()
-    t0 = time.perf_counter()
-    for _ in range(steps):
+    for _ in range(max(1, warmup)):
         step()
-    dt = (time.perf_counter() - t0) / steps
+    n = 0
+    t0 = time.perf_counter()
+    while True:
+        step()
+        n += 1
+        if (steps is not None and n >= steps) or (
+                steps is None and n >= 3 and time.perf_counter() - t0 >= CPU_MIN_SECONDS):
+            break
+    dt = (time.perf_counter() - t0) / n
     px = CPU_SAMPLE[0] * CPU_SAMPLE[1] * CPU_SAMPLE[2] * CPU_SAMPLE[3]
     return {"value": px * PRIMS / dt / 1e9, "unit": "Gpix/s", "cores": torch.get_num_threads(), "kind": kind,
-            "sample": f"x{CPU_SAMPLE} (one 4-channel slice of the 32x64 batch), dilation+erosion fwd+bwd, "
-                      f"{steps} step(s) after 1 warm-up, {dt:.2f} s/step; Gpix/s scales linearly in pixels",
+            "sample": f"x{CPU_SAMPLE} (one image of the 32x64x512x512 batch), dilation+erosion fwd+bwd with the "
+                      f"reference's CPU operators, {n} step(s) after {max(1, warmup)} warm-up, {dt:.2f} s/step; "
+                      f"Gpix/s scales linearly in pixels",
             "ms_per_step_sample": dt * 1e3}
 
 
@@ -158,11 +167,11 @@ def run_reference(args) -> None:
     world, rank, _ = _dist()
     if rank != 0:
         return
-    steps = max(1, min(args.steps, 3))
-    base = _cpu_baseline(steps)
+    steps, warmup = max(1, args.steps), max(1, args.warmup)
+    base = _cpu_baseline(steps, warmup)
     line = {
         "impl": "reference", "metric": METRIC, "value": base["value"], "unit": "Gpix/s", "n_gpus": args.gpus,
-        "steps": steps, "warmup": 1, "ms_per_step": base["ms_per_step_sample"], "higher_is_better": True,
+        "steps": steps, "warmup": warmup, "ms_per_step": base["ms_per_step_sample"], "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
         "config": {"workload": WORKLOAD, "sample": list(CPU_SAMPLE)},
         "cpu_baseline": {k: base[k] for k in ("value", "unit", "cores", "kind", "sample")},
@@ -333,7 +342,7 @@ def run_ours(args) -> None:
             "clocks": clock_info,
         }
         if world == 1:
-            line["cpu_baseline"] = {k_: v for k_, v in _cpu_baseline(1).items() if k_ != "ms_per_step_sample"}
+            line["cpu_baseline"] = {k_: v for k_, v in _cpu_baseline().items() if k_ != "ms_per_step_sample"}
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
