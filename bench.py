@@ -349,6 +349,121 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def _config_inputs(cfg: int, dev: torch.device):
+    """Synthetic inputs of the other workloads (shapes, distributions and seeds of their definitions)."""
+    import serron_b200 as serron
+
+    se = serron.structuring_element
+    g = torch.Generator(device=dev).manual_seed(0)
+    if cfg == 1:
+        x = torch.rand(1, 1, 256, 256, generator=torch.Generator().manual_seed(0)).to(dev)
+        return {"x": x, "k": se.disk(3, device=dev)}
+    if cfg == 3:
+        x = torch.rand(64, 32, 256, 256, device=dev, generator=g).to(torch.bfloat16)
+        w = torch.randn(32, 7, 7, device=dev, generator=g) * 0.1
+        return {"x": x, "w": w, "g": g}
+    if cfg == 4:
+        x = torch.rand(8, 3, 1024, 1024, device=dev, generator=g).to(torch.float16)
+        go = [torch.randn(8, 3, 1024, 1024, device=dev, generator=g).to(torch.float16) for _ in range(3)]
+        return {"x": x, "go": go, "k": se.disk(15, dtype=torch.float16, device=dev)}
+    # cfg 5: the smooth mask (64 separable Gaussians plus noise) and a 32-point marker, built on the CPU
+    cg = torch.Generator().manual_seed(0)
+    n = 8192
+    cy, cx = torch.rand(64, generator=cg) * n, torch.rand(64, generator=cg) * n
+    sigma, amp = 20 + 180 * torch.rand(64, generator=cg), torch.rand(64, generator=cg)
+    ax = torch.arange(n, dtype=torch.float64)
+    gy = torch.exp(-((ax[None, :] - cy[:, None].double()) ** 2) / (2 * sigma[:, None].double() ** 2))
+    gx = torch.exp(-((ax[None, :] - cx[:, None].double()) ** 2) / (2 * sigma[:, None].double() ** 2))
+    mask = torch.einsum("k,ky,kx->yx", amp.double(), gy, gx).float().view(1, 1, n, n)
+    mask += 0.05 * torch.rand(1, 1, n, n, generator=cg)
+    marker = torch.zeros_like(mask)
+    idx = torch.randperm(n * n, generator=cg)[:32]
+    marker.view(-1)[idx] = mask.view(-1)[idx]
+    return {"marker": marker.to(dev), "mask": mask.to(dev), "k": se.cross(3, device=dev)}
+
+
+def run_config(args) -> None:
+    """The other workloads, one GPU, device time per step (reported in the design notes, not by the driver)."""
+    import serron_b200 as serron
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    from serron_b200 import _lib
+
+    _lib.load()
+    cfg = args.config
+    d = _config_inputs(cfg, dev)
+    B = serron.BorderMode
+    if cfg == 1:
+        x, k = d["x"], d["k"]
+        prims, px, bytes_px = 2, x.numel(), 8
+
+        def step():
+            serron.dilation(serron.erosion(x, k, border=B.REPLICATE), k, border=B.REPLICATE)
+    elif cfg == 3:
+        layer = serron.Opening2d(32, 7).to(dev)
+        with torch.no_grad():
+            layer.weight.copy_(d["w"])
+        x = d["x"].requires_grad_(True)
+        with torch.autocast("cuda"):
+            y0 = layer(x)
+        go = torch.randn(y0.shape, device=dev, generator=d["g"]).to(torch.float16)
+        prims, px, bytes_px = 2, x.numel(), 10
+
+        def step():
+            with torch.autocast("cuda"):
+                y = layer(x)
+            torch.autograd.grad(y, (x, layer.weight), go)
+    elif cfg == 4:
+        x, k, gos = d["x"].requires_grad_(True), d["k"], d["go"]
+        prims, px, bytes_px = 6, x.numel(), 12
+
+        def step():
+            for fn, go in zip((serron.gradient, serron.top_hat, serron.black_hat), gos):
+                y = fn(x, k, border=B.CONSTANT)
+                torch.autograd.grad(y, x, go)
+    else:
+        marker, mask, k = d["marker"], d["mask"], d["k"]
+        prims, px, bytes_px = 1, mask.numel(), 12
+
+        def step():
+            serron.reconstruction_by_dilation(marker, mask, k, border=B.CONSTANT)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / args.steps
+    peak, peak_kind = _peaks()
+    line = {"config": cfg, "metric": "output Gpix/s" if cfg != 5 else "ms to the fixed point",
+            "value": px * prims / (ms * 1e-3) / 1e9 if cfg != 5 else ms, "ms_per_step": ms, "steps": args.steps,
+            "warmup": args.warmup, "pixels": px, "primitive_calls": prims,
+            "hbm_frac_of_algorithmic": (px * prims * bytes_px / (ms * 1e-3) / 1e9) / peak if cfg != 5 else None,
+            "peak_gbs": peak, "peak_source": peak_kind}
+    print(json.dumps(line), flush=True)
+
+
+def run_minmax_rate() -> None:
+    """Measured element min/max rate of the GPU: the compute roofline of the compare-select work."""
+    import ctypes
+
+    lib = ctypes.CDLL(os.path.join(REPO, "serron_b200", "libserron_minmax_rate.so"))
+    lib.serron_measure_minmax_rate.argtypes = [ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_double)]
+    out = {}
+    for kind, name in ((0, "fp32"), (1, "half2"), (2, "bfloat162")):
+        v = ctypes.c_double()
+        rc = lib.serron_measure_minmax_rate(kind, 0, ctypes.byref(v))
+        if rc:
+            raise RuntimeError(f"min/max rate measurement failed ({rc})")
+        out[name] = v.value / 1e12
+    print(json.dumps({"metric": "element min/max per second", "unit": "T/s", **out}), flush=True)
+
+
 def main() -> None:
     p = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     p.add_argument("--gpus", type=int, default=1)
@@ -357,8 +472,15 @@ def main() -> None:
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
     # a smaller leading dimension, for profiling captures that must stay within a few GB of device memory
     p.add_argument("--batch", type=int, default=SHAPE[0])
+    # the other workloads (1, 3, 4, 5) for the design notes; the default run is workload 2
+    p.add_argument("--config", type=int, choices=[1, 2, 3, 4, 5], default=2)
+    p.add_argument("--minmax-rate", action="store_true", help="measure the min/max issue rate and exit")
     args = p.parse_args()
-    if args.impl == "reference":
+    if args.minmax_rate:
+        run_minmax_rate()
+    elif args.config != 2:
+        run_config(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)

@@ -261,7 +261,7 @@ int format_bytes(int fmt) {
 bool format_is_separable(int fmt) { return base_format(fmt) >= SERRON_WINNERS_SEPARABLE_U8; }
 
 size_t tiled_smem_bytes(int64_t kH, int64_t kW, int dtype) {
-    return static_cast<size_t>((kTile + kH - 1) * (kTile + kW - 1) + kH * kW) * acc_size(dtype);
+    return tiled_smem(static_cast<int>(kH), static_cast<int>(kW), acc_size(dtype));
 }
 size_t sep_smem_bytes(int64_t kH, int64_t kW, int dtype) {
     return dtype == kF64 ? SepSmem<double>::bytes(static_cast<int>(kH), static_cast<int>(kW))

@@ -9,6 +9,8 @@
 // exactly the order and precision the reference CPU forms it, with no atomics.
 #pragma once
 
+#include <limits>
+
 #include "common.cuh"
 
 namespace serron {
@@ -118,8 +120,22 @@ __global__ void __launch_bounds__(256) element_fwd_kernel(const T* __restrict__ 
 
 // ------------------------------------------------------------------------------------------------
 // tiled forward (algo = tiled): a 32x32 output tile, its halo staged once in shared memory with the
-// border resolved at staging (CONSTANT cells hold the neutral element, which never wins)
+// border resolved at staging (CONSTANT cells hold the neutral element, which never wins).
+//
+// A thread computes four adjacent outputs of one row: for each SE row it walks the columns with a
+// sliding window of four samples in registers, so one shared-memory load and one (broadcast) weight
+// load serve four taps.  An SE row is walked only over its span of finite weights: a -inf weight never
+// wins (x + -inf for dilation, x - -inf for erosion), which skips most of a mask SE's corners.
 // ------------------------------------------------------------------------------------------------
+constexpr int kTileQuad = 4;  // adjacent outputs per thread
+
+// staged row pitch: odd, so that the 4 rows x 8 column groups of a warp hit distinct banks
+__host__ __device__ inline int tiled_pitch(int kW) { return (kTile + kW - 1) | 1; }
+__host__ __device__ inline size_t tiled_smem(int kH, int kW, size_t acc) {
+    return (static_cast<size_t>(kTile + kH - 1) * tiled_pitch(kW) + static_cast<size_t>(kH) * kW) * acc +
+           static_cast<size_t>(kH) * 2 * sizeof(int);
+}
+
 template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX>
 __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                         T* __restrict__ y, I* __restrict__ win, int C, int H, int W,
@@ -127,9 +143,10 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
                                                         int tiles_y) {
     using A = typename Storage<T>::acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    const int sw = kTile + kW - 1, sh = kTile + kH - 1;
+    const int sw = tiled_pitch(kW), sh = kTile + kH - 1;
     A* xs = reinterpret_cast<A*>(smem_raw);
     A* ws = xs + sw * sh;
+    int* span = reinterpret_cast<int*>(ws + kH * kW);  // [kH][2]: first and last finite column of an SE row
     __shared__ int exact_flag;
 
     const TileCoord tc = tile_coord(tiles_x, tiles_y);
@@ -140,6 +157,7 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
     const T* wc = w + static_cast<long long>(c) * kcs;
     const int tid = threadIdx.y * kTile + threadIdx.x;
     const A neutral = Op<OP>::template neutral<A>();
+    const A never = -std::numeric_limits<A>::infinity();  // a weight that never wins
 
     if (tid == 0) exact_flag = 1;
     __syncthreads();
@@ -148,36 +166,80 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
         ws[i] = v;
         if (NeedsExactCheck<T>::value && !weight_is_exact(static_cast<float>(v))) exact_flag = 0;
     }
-    for (int i = tid; i < sw * sh; i += 256) {
-        const int r = i / sw, q = i - r * sw;
+    const int cw = kTile + kW - 1;  // staged columns (the pitch may add one)
+    for (int i = tid; i < sh * cw; i += 256) {
+        const int r = i / cw, q = i - r * cw;
         int gr = oh0 - aH + r, gq = ow0 - aW + q;
         A v = neutral;
         if (resolve(gr, H, border) && resolve(gq, W, border)) v = Storage<T>::load(xp[static_cast<long long>(gr) * W + gq]);
-        xs[i] = v;
+        xs[r * sw + q] = v;
+    }
+    __syncthreads();
+    for (int di = tid; di < kH; di += 256) {
+        int lo = kW, hi = -1;
+        for (int dj = 0; dj < kW; ++dj)
+            if (!(ws[di * kW + dj] == never)) {
+                lo = min(lo, dj);
+                hi = dj;
+            }
+        span[2 * di] = lo;
+        span[2 * di + 1] = hi;
     }
     __syncthreads();
 
-    const int ow = ow0 + threadIdx.x;
+    const int lr = tid >> 3, q0 = (tid & 7) * kTileQuad;  // output row, first of four columns
+    const int oh = oh0 + lr;
+    if (oh >= H || ow0 + q0 >= W) return;
     const bool exact = !NeedsExactCheck<T>::value || exact_flag;
+    A best[kTileQuad];
+    int tap[kTileQuad];
+    bool tie[kTileQuad];
 #pragma unroll
-    for (int i = 0; i < kRowsPerThread; ++i) {
-        const int lr = threadIdx.y * kRowsPerThread + i;
-        const int oh = oh0 + lr;
-        if (oh >= H || ow >= W) continue;
-        auto sample = [&](int di, int dj, A& s) {
-            s = xs[(lr + di) * sw + threadIdx.x + dj];
-            return true;
-        };
-        auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
-        A best;
-        int tap;
-        if (exact)
-            window_winner<T, OP, false>(sample, weight, kH, kW, best, tap);
-        else
-            window_winner<T, OP, true>(sample, weight, kH, kW, best, tap);
+    for (int k = 0; k < kTileQuad; ++k) {
+        best[k] = neutral;
+        tap[k] = -1;
+        tie[k] = false;
+    }
+    for (int di = 0; di < kH; ++di) {
+        const int lo = span[2 * di], hi = span[2 * di + 1];
+        if (hi < lo) continue;
+        const A* row = xs + (lr + di) * sw + q0 + lo;
+        const A* wrow = ws + di * kW;
+        A s0 = row[0], s1 = row[1], s2 = row[2];
+        for (int dj = lo; dj <= hi; ++dj) {
+            const A s3 = row[dj - lo + 3];
+            const A wv = wrow[dj];
+            const A v[kTileQuad] = {Op<OP>::tap(s0, wv), Op<OP>::tap(s1, wv), Op<OP>::tap(s2, wv), Op<OP>::tap(s3, wv)};
+#pragma unroll
+            for (int k = 0; k < kTileQuad; ++k) {
+                if (!exact) tie[k] |= v[k] == best[k];
+                if (Op<OP>::better(v[k], best[k])) {
+                    best[k] = v[k];
+                    tap[k] = di * kW + dj;
+                }
+            }
+            s0 = s1;
+            s1 = s2;
+            s2 = s3;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < kTileQuad; ++k) {
+        const int ow = ow0 + q0 + k;
+        if (ow >= W) break;
+        if (!exact && tie[k] && best[k] != neutral) {
+            // a float tie with the running best: settle it the way the reference CPU does, in double
+            auto sample = [&](int di, int dj, A& s_) {
+                s_ = xs[(lr + di) * sw + q0 + k + dj];
+                return true;
+            };
+            auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
+            A b_;
+            window_winner<T, OP, true>(sample, weight, kH, kW, b_, tap[k]);
+        }
         const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
-        if (WITH_VALUE) y[o] = Storage<T>::store(best);
-        if (WITH_INDEX) win[o] = encode_direct<I>(tap);
+        if (WITH_VALUE) y[o] = Storage<T>::store(best[k]);
+        if (WITH_INDEX) win[o] = encode_direct<I>(tap[k]);
     }
 }
 
