@@ -477,17 +477,14 @@ SegradPlan segrad_plan(const Geometry& g) {
     SegradPlan p;
     const int64_t bins = g.kH * g.kW;
     const int64_t per_channel = g.N * g.H * g.W;
-    const int64_t max_chunks = std::max<int64_t>(1, 592 / std::max<int64_t>(g.C, 1));
+    p.threads = bins <= 96 ? 128 : 32;
+    p.global_bins = bins > 768;
+    // about 32 chunks per SM over all channels, enough threads in flight to hide the loads, with the
+    // partials held to 4 MiB; per-thread bins in global memory keep the old 4 chunks per SM
+    const int64_t total_chunks = p.global_bins ? 592 : std::min<int64_t>(4736, (int64_t(4) << 20) / (bins * 8));
+    const int64_t max_chunks = std::max<int64_t>(1, total_chunks / std::max<int64_t>(g.C, 1));
     p.chunks = static_cast<int>(std::clamp<int64_t>((per_channel + 16383) / 16384, 1, max_chunks));
     p.per_chunk = (per_channel + p.chunks - 1) / p.chunks;
-    if (bins <= 96) {
-        p.threads = 128;
-    } else if (bins <= 768) {
-        p.threads = 32;
-    } else {
-        p.threads = 32;
-        p.global_bins = true;
-    }
     p.partial_bytes = g.C * p.chunks * bins * 8;
     p.bins_bytes = p.global_bins ? g.C * p.chunks * int64_t(p.threads) * bins * 8 : 0;
     return p;
@@ -591,7 +588,7 @@ void launch_segrad_t(int op, const Geometry& g, const void* go, const void* win,
     SB_CUDA(cudaGetLastError());
     const int out_cells = static_cast<int>(g.kcs ? g.C * bins : bins);
     const double sign = op == kErode ? -1.0 : 1.0;
-    segrad_final_kernel<T><<<ceil_div(out_cells, 128), 128, 0, stream>>>(partial, static_cast<T*>(gk),
+    segrad_final_kernel<T><<<out_cells, kSegradFinalThreads, 0, stream>>>(partial, static_cast<T*>(gk),
                                                                           static_cast<int>(g.C), p.chunks, bins,
                                                                           g.kcs ? 0 : 1, sign);
     SB_CUDA(cudaGetLastError());

@@ -345,7 +345,7 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
     constexpr int TP = kSumTP, TQ = kPullTQ, NT = kSumThreads, NWORDS = TP * TQ / 32;
     constexpr uint32_t kNone = IndexTraits<I>::none;
     const SumGeom geo(kH, kW, sizeof(T), sizeof(I));
-    const int aH = geo.aH, aW = geo.aW, hr = geo.hr, hq = geo.hq, gv = geo.gv, goff = geo.goff, gq = geo.gq;
+    const int aH = geo.aH, aW = geo.aW, hq = geo.hq, gv = geo.gv, goff = geo.goff, gq = geo.gq;
     const int rv = geo.rv, roff = geo.roff, rq = geo.rq;
     const int S = 2 * aW + 1;
     extern __shared__ __align__(16) unsigned char smem_raw[];

@@ -42,12 +42,45 @@ __global__ void segrad_partial_kernel(const T* __restrict__ go, const I* __restr
     const long long total = static_cast<long long>(N) * hw;
     const long long start = blockIdx.x * per_chunk;
     const long long end = min(start + per_chunk, total);
-    for (long long e = start + tid; e < end; e += nthr) {
-        const long long n = e / hw, s = e - n * hw;
-        const long long plane_base = (n * C + c) * hw;
-        const int oh = static_cast<int>(s / W), ow = static_cast<int>(s - static_cast<long long>(oh) * W);
-        const int t = winner_tap<I, SEP>(win, plane_base, oh, ow, H, W, kH, kW, border);
-        if (t >= 0) mine[t] += static_cast<double>(Storage<T>::load(go[plane_base + s]));
+    long long e = start + tid;
+    if (e < end) {
+        // one division per thread; the position then advances by the block size.  Four outputs are
+        // read before any is accumulated, so each thread keeps several loads in flight.
+        long long n = e / hw;
+        const long long s0 = e - n * hw;
+        int oh = static_cast<int>(s0 / W), ow = static_cast<int>(s0 - static_cast<long long>(oh) * W);
+        long long plane_base = (n * C + c) * hw;
+        auto advance = [&]() {
+            ow += nthr;
+            while (ow >= W) {
+                ow -= W;
+                if (++oh == H) {
+                    oh = 0;
+                    ++n;
+                    plane_base = (n * C + c) * hw;
+                }
+            }
+        };
+        constexpr int U = 4;
+        for (; e + (U - 1) * static_cast<long long>(nthr) < end; e += U * static_cast<long long>(nthr)) {
+            int t[U];
+            double v[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+                t[u] = winner_tap<I, SEP>(win, plane_base, oh, ow, H, W, kH, kW, border);
+                v[u] = static_cast<double>(Storage<T>::load(go[plane_base + static_cast<long long>(oh) * W + ow]));
+                advance();
+            }
+#pragma unroll
+            for (int u = 0; u < U; ++u)
+                if (t[u] >= 0) mine[t[u]] += v[u];
+        }
+        for (; e < end; e += nthr) {
+            const int t = winner_tap<I, SEP>(win, plane_base, oh, ow, H, W, kH, kW, border);
+            if (t >= 0)
+                mine[t] += static_cast<double>(Storage<T>::load(go[plane_base + static_cast<long long>(oh) * W + ow]));
+            advance();
+        }
     }
     __syncthreads();
     if (bins_global) __threadfence_block();
@@ -59,22 +92,32 @@ __global__ void segrad_partial_kernel(const T* __restrict__ go, const I* __restr
     }
 }
 
-// gk[cell] = sign * sum over chunks (and over channels for a shared SE) of the partials, in order.
+// gk[cell] = sign * sum over chunks (and over channels for a shared SE) of the partials.  One CTA per
+// output cell: thread i sums the partials i, i + 128, ... in order, then the 128 sums are added by a
+// fixed tree, so the result does not depend on scheduling.
+constexpr int kSegradFinalThreads = 128;
 template <typename T>
-__global__ void segrad_final_kernel(const double* __restrict__ partial, T* __restrict__ gk, int C, int chunks,
-                                    int bins, int shared, double sign) {
-    const int cell = blockIdx.x * blockDim.x + threadIdx.x;
-    const int out_cells = shared ? bins : C * bins;
-    if (cell >= out_cells) return;
+__global__ void __launch_bounds__(kSegradFinalThreads) segrad_final_kernel(const double* __restrict__ partial,
+                                                                           T* __restrict__ gk, int C, int chunks,
+                                                                           int bins, int shared, double sign) {
+    __shared__ double red[kSegradFinalThreads];
+    const int cell = blockIdx.x, tid = threadIdx.x;
     double acc = 0.0;
     if (shared) {
-        for (int c = 0; c < C; ++c)
-            for (int k = 0; k < chunks; ++k) acc += partial[(static_cast<long long>(c) * chunks + k) * bins + cell];
+        const int total = C * chunks;
+        for (int j = tid; j < total; j += kSegradFinalThreads) acc += partial[static_cast<long long>(j) * bins + cell];
     } else {
         const int c = cell / bins, b = cell - c * bins;
-        for (int k = 0; k < chunks; ++k) acc += partial[(static_cast<long long>(c) * chunks + k) * bins + b];
+        for (int k = tid; k < chunks; k += kSegradFinalThreads)
+            acc += partial[(static_cast<long long>(c) * chunks + k) * bins + b];
     }
-    gk[cell] = Storage<T>::store(static_cast<typename Storage<T>::acc>(sign * acc));
+    red[tid] = acc;
+    __syncthreads();
+    for (int half = kSegradFinalThreads / 2; half > 0; half >>= 1) {
+        if (tid < half) red[tid] += red[tid + half];
+        __syncthreads();
+    }
+    if (tid == 0) gk[cell] = Storage<T>::store(static_cast<typename Storage<T>::acc>(sign * red[0]));
 }
 
 }  // namespace serron
