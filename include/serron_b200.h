@@ -176,10 +176,13 @@ SERRON_API int64_t serron_get_separable_min_k(int32_t device, int32_t dtype, int
  * Geodesic reconstruction.  Replaces the Python loop of serron.functional._reconstruct
  * (packages/serron/torch-ext/serron/functional.py:144-202): out = the fixed point of
  * clip(step(y), mask) from y = clip(marker, mask), step = dilate/clip = min when dilate != 0, else
- * erode/max.  With max_iter <= 0 the fixed point is found by tile-local relaxation; with max_iter > 0
+ * erode/max.  With max_iter <= 0 the fixed point is found by row and column scans (flat SEs) and
+ * tile-local relaxation over the tiles whose halo moved; with max_iter > 0
  * the reference's Jacobi schedule and check_every test are reproduced, so the call fails exactly when
  * the reference would.  Synchronous (reads a convergence flag).  *steps receives the number of
- * launches (relaxation) or Jacobi steps taken.  Workspace: serron_reconstruct_workspace_bytes.
+ * scan rounds and relaxation launches, or Jacobi steps, taken.  Workspace:
+ * serron_reconstruct_workspace_bytes (256 bytes of flags, then one byte per 64x64 tile for max_iter <= 0
+ * or a second image for max_iter > 0).
  * --------------------------------------------------------------------------------------------- */
 SERRON_API int serron_reconstruct(int32_t dilate, const void* marker, const void* mask, const int64_t* sizes,
                                   int64_t dim, const void* kernel, const int64_t* kernel_sizes, int64_t kernel_dim,

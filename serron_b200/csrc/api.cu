@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "direct.cuh"
 #include "recon.cuh"
+#include "recon_scan.cuh"
 #include "segrad.cuh"
 #include "separable.cuh"
 #include "gather_pull.cuh"
@@ -335,6 +336,8 @@ void dispatch_index(int fmt, F&& f) {
     }
 }
 
+constexpr size_t kSmemOptin = 227 * 1024;  // sm_100 shared memory per CTA with the opt-in
+
 template <typename K>
 void set_smem(K kernel, size_t bytes) {
     if (bytes > 48 * 1024) SB_CUDA(cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(bytes)));
@@ -363,12 +366,22 @@ bool launch_forward_t(int algo, const Geometry& g, const void* x, const void* w,
         element_fwd_kernel<T, OP, I, V, X><<<grid_1d((total + 255) / 256), 256, 0, stream>>>(
             xp, wp, yp, ip, total, C, H, W, kH, kW, kcs, border);
     } else if (algo == kTiled) {
-        const int tx = ceil_div(W, kTile), ty = ceil_div(H, kTile);
-        const size_t smem = tiled_smem_bytes(kH, kW, std::is_same<T, double>::value ? kF64 : kF32);
-        auto kernel = tiled_fwd_kernel<T, OP, I, V, X>;
-        set_smem(kernel, smem);
-        kernel<<<grid_1d(static_cast<long long>(tx) * ty * g.N * g.C), dim3(kTile, kTileThreadsY), smem, stream>>>(
-            xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty);
+        const size_t acc = sizeof(typename Storage<T>::acc);
+        if (kW >= kWideQ + 1 && wide_smem(kH, kW, acc) <= kSmemOptin) {
+            const int tx = ceil_div(W, kWideCols), ty = ceil_div(H, kWideRows);
+            const size_t smem = wide_smem(kH, kW, acc);
+            auto kernel = wide_fwd_kernel<T, OP, I, V, X>;
+            set_smem(kernel, smem);
+            kernel<<<grid_1d(static_cast<long long>(tx) * ty * g.N * g.C), 256, smem, stream>>>(
+                xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty);
+        } else {
+            const int tx = ceil_div(W, kTile), ty = ceil_div(H, kTile);
+            const size_t smem = tiled_smem_bytes(kH, kW, std::is_same<T, double>::value ? kF64 : kF32);
+            auto kernel = tiled_fwd_kernel<T, OP, I, V, X>;
+            set_smem(kernel, smem);
+            kernel<<<grid_1d(static_cast<long long>(tx) * ty * g.N * g.C), dim3(kTile, kTileThreadsY), smem, stream>>>(
+                xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty);
+        }
     } else {
         if constexpr (!std::is_same<T, double>::value) {
             if (kH == kW && g.N * g.C < (1ll << 31) / 4096 && g.H * g.W < (1ll << 31)) {
@@ -715,18 +728,22 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
         const int H = static_cast<int>(g.H), W = static_cast<int>(g.W), C = static_cast<int>(g.C);
         const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW), kcs = static_cast<int>(g.kcs);
         const int op = dilate ? kDilate : kErode;
-        int host_flags[2] = {0, 0};
+        int host_flags[3] = {0, 0, 0};
         int64_t taken = 0;
         bool converged = false;
         dispatch_dtype(dtype, [&](auto t) {
             using T = decltype(t);
             dispatch_op(op, [&](auto o) {
                 constexpr int OP = decltype(o)::value;
-                SB_CUDA(cudaMemsetAsync(flags, 0, 2 * sizeof(int), stream));
+                SB_CUDA(cudaMemsetAsync(flags, 0, 3 * sizeof(int), stream));
                 recon_init_kernel<T, OP><<<grid_1d((total + 255) / 256), 256, 0, stream>>>(
                     static_cast<const T*>(marker), static_cast<const T*>(mask), static_cast<T*>(output), total, flags);
                 SB_CUDA(cudaGetLastError());
-                SB_CUDA(cudaMemcpyAsync(host_flags, flags, 2 * sizeof(int), cudaMemcpyDeviceToHost, stream));
+                if (max_iter <= 0 && kcs == 0) {
+                    recon_se_class_kernel<T, OP><<<1, 32, 0, stream>>>(static_cast<const T*>(kernel), kH, kW, flags + 2);
+                    SB_CUDA(cudaGetLastError());
+                }
+                SB_CUDA(cudaMemcpyAsync(host_flags, flags, 3 * sizeof(int), cudaMemcpyDeviceToHost, stream));
                 SB_CUDA(cudaStreamSynchronize(stream));
                 const bool has_nan = host_flags[1] != 0;
                 if (max_iter <= 0) {
@@ -744,11 +761,51 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                     set_smem(kernel_fn, smem);
                     const long long blocks = static_cast<long long>(tx) * ty * g.N * g.C;
                     const int64_t cap = 4 * (static_cast<int64_t>(H) * W + 16);
-                    for (;;) {
+                    // a flat SE with an anchor and a direct neighbour: first rounds of row and column scans,
+                    // which carry fronts across the image; when only the scans' taps exist and a round
+                    // changes nothing, that is the fixed point
+                    const int cls = host_flags[2];
+                    const int lines = cls & (kScanLeft | kScanRight | kScanUp | kScanDown);
+                    if ((cls & kScanFlat) && lines) {
+                        using A = typename Storage<T>::acc;
+                        const size_t row_smem = 2 * static_cast<size_t>(kScanChunk) * sizeof(A);
+                        auto rows_fn = recon_rows_kernel<T, OP>;
+                        set_smem(rows_fn, row_smem);
+                        const int strips = ceil_div(W, kScanCols);
+                        const long long rows = g.N * g.C * g.H, strip_blocks = g.N * g.C * strips;
+                        // under REFLECT a one-sided line tap at the image edge reads the pixel on its other
+                        // side, which only the opposite scan covers
+                        const bool lop = ((cls & kScanLeft) != 0) != ((cls & kScanRight) != 0);
+                        const bool vop = ((cls & kScanUp) != 0) != ((cls & kScanDown) != 0);
+                        const bool complete = !(cls & kScanOther) && !(border == kReflect && (lop || vop));
+                        for (int round = 0; round < kScanRounds; ++round) {
+                            SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
+                            if (lines & (kScanLeft | kScanRight))
+                                rows_fn<<<grid_1d(rows), kScanThreads, row_smem, stream>>>(
+                                    static_cast<T*>(output), static_cast<const T*>(mask), W, cls, flags);
+                            if (lines & (kScanUp | kScanDown))
+                                recon_cols_kernel<T, OP><<<grid_1d(strip_blocks), kScanThreads, 0, stream>>>(
+                                    static_cast<T*>(output), static_cast<const T*>(mask), H, W, strips, cls, flags);
+                            SB_CUDA(cudaGetLastError());
+                            ++taken;
+                            SB_CUDA(cudaMemcpyAsync(host_flags, flags, sizeof(int), cudaMemcpyDeviceToHost, stream));
+                            SB_CUDA(cudaStreamSynchronize(stream));
+                            if (host_flags[0] == 0) {
+                                converged = complete;
+                                break;
+                            }
+                        }
+                    }
+                    // then tile relaxation to the fixed point; when a tile's halo reaches only its eight
+                    // neighbours, a launch runs only the tiles whose halo moved
+                    const bool worklist = kH < kRecTile && kW < kRecTile && H > kH && W > kW;
+                    uint8_t* dirty = worklist ? static_cast<uint8_t*>(tmp) : nullptr;
+                    if (dirty && !converged) SB_CUDA(cudaMemsetAsync(dirty, 1, blocks, stream));
+                    while (!converged) {
                         SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
                         kernel_fn<<<grid_1d(blocks), kRecThreads, smem, stream>>>(
                             static_cast<T*>(output), static_cast<const T*>(mask), static_cast<const T*>(kernel), C, H,
-                            W, kH, kW, kcs, static_cast<int>(border), tx, ty, 4 * kRecTile, flags);
+                            W, kH, kW, kcs, static_cast<int>(border), tx, ty, 4 * kRecTile, flags, dirty);
                         SB_CUDA(cudaGetLastError());
                         ++taken;
                         SB_CUDA(cudaMemcpyAsync(host_flags, flags, sizeof(int), cudaMemcpyDeviceToHost, stream));
@@ -1017,7 +1074,9 @@ int serron_reconstruct(int32_t dilate, const void* marker, const void* mask, con
 int64_t serron_reconstruct_workspace_bytes(const int64_t* sizes, int64_t dim, int32_t dtype, int64_t max_iter) {
     if (dim != 4 || sizes == nullptr || dtype < kF32 || dtype > kBF16) return -1;
     const int64_t total = sizes[0] * sizes[1] * sizes[2] * sizes[3];
-    return 256 + (max_iter > 0 ? align256(total * static_cast<int64_t>(elem_size(dtype))) : 0);
+    // the Jacobi schedule's second buffer, or one dirty byte per relaxation tile
+    const int64_t tiles = sizes[0] * sizes[1] * ((sizes[2] + kRecTile - 1) / kRecTile) * ((sizes[3] + kRecTile - 1) / kRecTile);
+    return 256 + (max_iter > 0 ? align256(total * static_cast<int64_t>(elem_size(dtype))) : align256(tiles));
 }
 
 }  // extern "C"

@@ -244,6 +244,193 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
 }
 
 // ------------------------------------------------------------------------------------------------
+// wide tiled forward (algo = tiled, windows 9 or more columns wide): a 32x64 output tile, eight
+// adjacent outputs per thread.  An SE row whose span holds one weight of zero (every row of a flat
+// disk, diamond or square) needs no per-tap weight: the eight windows over that row share the core
+// [c0 + lo + 7, c0 + hi], so the thread takes the core's first extremum once, suffix extrema of the
+// seven columns left of it and prefix extrema of the seven right of it, and combines three
+// candidates per output in column order (ties keep the leftmost): span + 27 compare-selects for
+// eight outputs instead of 8 x span.  Other rows are walked like tiled_fwd_kernel, eight samples in
+// registers.  NaN samples are staged as the neutral element (neither wins).
+// ------------------------------------------------------------------------------------------------
+constexpr int kWideRows = 32, kWideCols = 64, kWideQ = 8;
+
+__host__ __device__ inline int wide_pitch(int kW) { return (kWideCols + kW - 1) | 1; }
+__host__ __device__ inline size_t wide_smem(int kH, int kW, size_t acc) {
+    return (static_cast<size_t>(kWideRows + kH - 1) * wide_pitch(kW) + static_cast<size_t>(kH) * kW) * acc +
+           static_cast<size_t>(kH) * 3 * sizeof(int);
+}
+
+template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX>
+__global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
+                                                       T* __restrict__ y, I* __restrict__ win, int C, int H, int W,
+                                                       int kH, int kW, int kcs, int border, int tiles_x,
+                                                       int tiles_y) {
+    using A = typename Storage<T>::acc;
+    constexpr int Q = kWideQ;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    const int sw = wide_pitch(kW), sh = kWideRows + kH - 1;
+    A* xs = reinterpret_cast<A*>(smem_raw);
+    A* ws = xs + sw * sh;
+    int* info = reinterpret_cast<int*>(ws + kH * kW);  // [kH][3]: first and last finite column, one weight
+    __shared__ int exact_flag;
+
+    const TileCoord tc = tile_coord(tiles_x, tiles_y);
+    const int c = static_cast<int>(tc.plane % C);
+    const int oh0 = tc.ty * kWideRows, ow0 = tc.tx * kWideCols;
+    const int aH = kH / 2, aW = kW / 2;
+    const T* xp = x + tc.plane * H * W;
+    const T* wc = w + static_cast<long long>(c) * kcs;
+    const int tid = threadIdx.x;
+    const A neutral = Op<OP>::template neutral<A>();
+    const A never = -std::numeric_limits<A>::infinity();
+
+    if (tid == 0) exact_flag = 1;
+    __syncthreads();
+    for (int i = tid; i < kH * kW; i += 256) {
+        const A v = Storage<T>::load(wc[i]);
+        ws[i] = v;
+        if (NeedsExactCheck<T>::value && !weight_is_exact(static_cast<float>(v))) exact_flag = 0;
+    }
+    const int cw = kWideCols + kW - 1;
+    for (int i = tid; i < sh * cw; i += 256) {
+        const int r = i / cw, q = i - r * cw;
+        int gr = oh0 - aH + r, gq = ow0 - aW + q;
+        A v = neutral;
+        if (resolve(gr, H, border) && resolve(gq, W, border)) v = Storage<T>::load(xp[static_cast<long long>(gr) * W + gq]);
+        xs[r * sw + q] = v != v ? neutral : v;
+    }
+    __syncthreads();
+    for (int di = tid; di < kH; di += 256) {
+        int lo = kW, hi = -1;
+        for (int dj = 0; dj < kW; ++dj)
+            if (!(ws[di * kW + dj] == never)) {
+                lo = min(lo, dj);
+                hi = dj;
+            }
+        // one weight over the whole span, of value zero (bit-identical, so the row's taps add the same)
+        bool one = hi >= lo && ws[di * kW + lo] == A(0);
+        for (int dj = lo; one && dj <= hi; ++dj)
+            one = ws[di * kW + dj] == A(0) && signbit(ws[di * kW + dj]) == signbit(ws[di * kW + lo]);
+        info[3 * di] = lo;
+        info[3 * di + 1] = hi;
+        info[3 * di + 2] = one ? 1 : 0;
+    }
+    __syncthreads();
+
+    const int lr = tid >> 3, c0 = (tid & 7) * Q;  // output row, first of eight columns
+    const int oh = oh0 + lr;
+    if (oh >= H || ow0 + c0 >= W) return;
+    const bool exact = !NeedsExactCheck<T>::value || exact_flag;
+    A best[Q];
+    int tap[Q];
+    bool tie[Q];
+#pragma unroll
+    for (int k = 0; k < Q; ++k) {
+        best[k] = neutral;
+        tap[k] = -1;
+        tie[k] = false;
+    }
+    for (int di = 0; di < kH; ++di) {
+        const int lo = info[3 * di], hi = info[3 * di + 1];
+        if (hi < lo) continue;
+        const A* row = xs + (lr + di) * sw + c0;  // output k's window starts at row[k]
+        const A* wrow = ws + di * kW;
+        if (info[3 * di + 2] && hi - lo + 1 >= Q) {
+            // suffix extrema of row[lo .. lo + Q - 2] (ties: the left one)
+            A sv[Q - 1];
+            int sc[Q - 1];
+            sv[Q - 2] = row[lo + Q - 2];
+            sc[Q - 2] = lo + Q - 2;
+#pragma unroll
+            for (int k = Q - 3; k >= 0; --k) {
+                const A v = row[lo + k];
+                const bool take = !Op<OP>::better(sv[k + 1], v);
+                sv[k] = take ? v : sv[k + 1];
+                sc[k] = take ? lo + k : sc[k + 1];
+            }
+            // core row[lo + Q - 1 .. hi], first extremum
+            A cv = row[lo + Q - 1];
+            int cc = lo + Q - 1;
+            for (int j = lo + Q; j <= hi; ++j) {
+                const A v = row[j];
+                if (Op<OP>::better(v, cv)) {
+                    cv = v;
+                    cc = j;
+                }
+            }
+            const A wz = wrow[lo];
+            A pv = neutral;
+            int pc = 0;
+#pragma unroll
+            for (int k = 0; k < Q; ++k) {
+                // window of output k: row[lo + k .. lo + Q - 2], the core, row[hi + 1 .. hi + k]
+                A rv = cv;
+                int rc = cc;
+                if (k < Q - 1 && !Op<OP>::better(cv, sv[k])) {
+                    rv = sv[k];
+                    rc = sc[k];
+                }
+                if (k > 0) {
+                    const A v = row[hi + k];
+                    if (k == 1 || Op<OP>::better(v, pv)) {
+                        pv = v;
+                        pc = hi + k;
+                    }
+                    if (Op<OP>::better(pv, rv)) {
+                        rv = pv;
+                        rc = pc;
+                    }
+                }
+                const A t = Op<OP>::tap(rv, wz);
+                if (!exact) tie[k] |= t == best[k];
+                if (Op<OP>::better(t, best[k])) {
+                    best[k] = t;
+                    tap[k] = di * kW + rc - k;
+                }
+            }
+        } else {
+            A s[Q];
+#pragma unroll
+            for (int k = 0; k < Q - 1; ++k) s[k] = row[lo + k];
+            for (int dj = lo; dj <= hi; ++dj) {
+                s[Q - 1] = row[dj + Q - 1];
+                const A wv = wrow[dj];
+#pragma unroll
+                for (int k = 0; k < Q; ++k) {
+                    const A v = Op<OP>::tap(s[k], wv);
+                    if (!exact) tie[k] |= v == best[k];
+                    if (Op<OP>::better(v, best[k])) {
+                        best[k] = v;
+                        tap[k] = di * kW + dj;
+                    }
+                }
+#pragma unroll
+                for (int k = 0; k < Q - 1; ++k) s[k] = s[k + 1];
+            }
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < Q; ++k) {
+        const int ow = ow0 + c0 + k;
+        if (ow >= W) break;
+        if (!exact && tie[k] && best[k] != neutral) {
+            // a float tie with the running best: settle it the way the reference CPU does, in double
+            auto sample = [&](int di, int dj, A& s_) {
+                s_ = xs[(lr + di) * sw + c0 + k + dj];
+                return true;
+            };
+            auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
+            A b_;
+            window_winner<T, OP, true>(sample, weight, kH, kW, b_, tap[k]);
+        }
+        const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
+        if (WITH_VALUE) y[o] = Storage<T>::store(best[k]);
+        if (WITH_INDEX) win[o] = encode_direct<I>(tap[k]);
+    }
+}
+
+// ------------------------------------------------------------------------------------------------
 // grad_input gather for direct winners
 //
 // Each CTA owns a 32x32 tile of input pixels and stages the winners and grad_output of every output

@@ -63,11 +63,17 @@ __global__ void recon_init_kernel(const T* __restrict__ marker, const T* __restr
     y[i] = Storage<T>::store(Clip<OP>::apply(a, m));
 }
 
+// With `dirty` (one byte per tile), a launch runs only the tiles flagged in it: a tile clears its flag
+// before reading, and a tile that changed flags its eight neighbours (after its writes are visible),
+// so a tile whose halo moved runs again in this launch or the next.  flags[0] is raised whenever a flag
+// is set; the host stops when a launch sets none.  Without `dirty` every tile runs and flags[0] says
+// whether anything changed.
 template <typename T, int OP>
 __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__ y, const T* __restrict__ mask,
                                                                  const T* __restrict__ w, int C, int H, int W, int kH,
                                                                  int kW, int kcs, int border, int tiles_x,
-                                                                 int tiles_y, int max_inner, int* __restrict__ flags) {
+                                                                 int tiles_y, int max_inner, int* __restrict__ flags,
+                                                                 uint8_t* __restrict__ dirty) {
     using A = typename Storage<T>::acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int aH = kH / 2, aW = kW / 2;
@@ -87,6 +93,18 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
     const int tid = threadIdx.x;
     const A neutral = Op<OP>::template neutral<A>();
 
+    if (dirty) {
+        __shared__ int run;
+        if (tid == 0) {
+            run = dirty[b];
+            if (run) {
+                dirty[b] = 0;
+                __threadfence();
+            }
+        }
+        __syncthreads();
+        if (!run) return;
+    }
     for (int i = tid; i < kH * kW; i += kRecThreads) ws[i] = Storage<T>::load(wc[i]);
     for (int i = tid; i < sw * sh; i += kRecThreads) {
         const int r = i / sw, q = i - r * sw;
@@ -120,7 +138,7 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
     };
     auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
 
-    bool any_change = false;
+    bool any_change = false, settled = false;
     for (int it = 0; it < max_inner; ++it) {
         bool changed = false;
         for (int i = tid; i < kRecTile * kRecTile; i += kRecThreads) {
@@ -136,7 +154,10 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
             }
         }
         changed = __syncthreads_or(changed);
-        if (!changed) break;
+        if (!changed) {
+            settled = true;
+            break;
+        }
         any_change = true;
     }
     if (any_change) {
@@ -144,6 +165,16 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
             const int lr = i / kRecTile, lq = i - lr * kRecTile;
             const int gr = h0 + lr, gq = w0 + lq;
             if (gr < H && gq < W) yp[static_cast<long long>(gr) * W + gq] = Storage<T>::store(ys[(lr + aH) * sw + lq + aW]);
+        }
+        if (dirty) {
+            __threadfence();
+            __syncthreads();
+            // the neighbours, and the tile itself when its inner iterations ran out before it settled
+            if (tid < 9 && (tid != 4 || !settled)) {
+                const int nx = tx + tid % 3 - 1, ny = ty + tid / 3 - 1;
+                if (nx >= 0 && nx < tiles_x && ny >= 0 && ny < tiles_y)
+                    dirty[plane * tiles_x * tiles_y + static_cast<long long>(ny) * tiles_x + nx] = 1;
+            }
         }
         if (tid == 0) atomicOr(flags, 1);
     }

@@ -1,0 +1,304 @@
+// Geodesic reconstruction by directional scans, for flat structuring elements.
+//
+// The reference (torch-ext/serron/functional.py:144-202) iterates y <- clip(step(y), mask) until
+// nothing changes.  Any schedule that keeps raising pixels to a value the full step could give them
+// reaches the same fixed point (recon.cuh states why), so these kernels raise whole rows and columns
+// at once.  For a flat element whose anchor row holds the left neighbour tap, the left-to-right
+// update of one row,
+//     y[c] <- C(m[c], B(y[c], y[c - 1]))        B = max, C = min for reconstruction by dilation,
+// is a composition of clamps f_c(x) = C(m[c], B(a[c], x)), and clamps compose into clamps using
+// selections only: g(f(x)) = C(g(fq), B(g(fp), x)) for f = (fp, fq), f(x) = C(fq, B(fp, x)).  So a
+// row scan is a parallel prefix over (p, q) pairs whose result is the sequential scan's, value for
+// value.  `recon_rows_kernel` runs left-to-right then right-to-left over each row, one CTA per row;
+// `recon_cols_kernel` runs top-to-bottom then bottom-to-top over 32-column strips, each warp holding
+// one run of rows.  A round of both carries a front across the image along any path that turns a
+// few times, where the tile relaxation moves it one tile per launch.  The host runs a few such rounds
+// and leaves the rest (paths that turn often, taps the scans do not cover) to recon_tile_kernel,
+// which also confirms the fixed point.
+//
+// Border taps are skipped by the scans (a partial update is still a valid one); where that leaves a
+// tap of the full step uncovered (REFLECT with a one-sided line tap, whose edge sample lies on the
+// other side) a round without change is not taken as the fixed point.  Inputs hold no NaN: the host
+// routes NaN inputs elsewhere before any scan runs.
+#pragma once
+
+#include "recon.cuh"
+
+namespace serron {
+
+constexpr int kScanThreads = 1024;
+constexpr int kScanPer = 8;                          // elements per thread in a row chunk
+constexpr int kScanChunk = kScanThreads * kScanPer;  // row chunk held in shared memory
+constexpr int kScanCols = 32;                        // columns per CTA of the column scan
+constexpr int kScanRounds = 8;                       // scan rounds before the tile relaxation takes over
+
+// SE classes found on the device (bits of flags[2])
+constexpr int kScanFlat = 1;     // every present tap has weight 0 and the anchor is present
+constexpr int kScanLeft = 2;     // tap sampling (row, column - 1)
+constexpr int kScanRight = 4;    // (row, column + 1)
+constexpr int kScanUp = 8;       // (row - 1, column)
+constexpr int kScanDown = 16;    // (row + 1, column)
+constexpr int kScanOther = 32;   // any other present tap
+
+// one step of the reconstruction as a clamp: f(x) = C(q, B(p, x))
+template <int OP>
+struct ReconClamp {
+    template <typename A>
+    static __device__ __forceinline__ A B(A a, A x) { return Op<OP>::better(x, a) ? x : a; }
+    template <typename A>
+    static __device__ __forceinline__ A C(A m, A v) { return Clip<OP>::apply(v, m); }
+    template <typename A>
+    static __device__ __forceinline__ A apply(A p, A q, A x) { return C(q, B(p, x)); }
+    // (p, q) <- g o f with f = (p, q) applied first
+    template <typename A>
+    static __device__ __forceinline__ void then(A& p, A& q, A gp, A gq) {
+        p = apply(gp, gq, p);
+        q = apply(gp, gq, q);
+    }
+};
+
+template <typename T, int OP>
+__global__ void recon_se_class_kernel(const T* __restrict__ w, int kH, int kW, int* __restrict__ out) {
+    using A = typename Storage<T>::acc;
+    if (threadIdx.x != 0 || blockIdx.x != 0) return;
+    const int aH = kH / 2, aW = kW / 2;
+    const A never = Op<kDilate>::template neutral<A>();  // a weight of -inf never wins
+    bool flat = true, anchor = false;
+    int cls = 0;
+    for (int di = 0; di < kH; ++di)
+        for (int dj = 0; dj < kW; ++dj) {
+            const A v = Storage<T>::load(w[di * kW + dj]);
+            if (v == never) continue;
+            if (!(v == A(0))) flat = false;
+            const int dr = di - aH, dc = dj - aW;
+            if (dr == 0 && dc == 0) anchor = true;
+            else if (dr == 0 && dc == -1) cls |= kScanLeft;
+            else if (dr == 0 && dc == 1) cls |= kScanRight;
+            else if (dr == -1 && dc == 0) cls |= kScanUp;
+            else if (dr == 1 && dc == 0) cls |= kScanDown;
+            else cls |= kScanOther;
+        }
+    if (flat && anchor) cls |= kScanFlat;
+    *out = cls;
+}
+
+// Block-wide exclusive prefix of the clamps (p, q) of all threads, in thread order, applied to `x`.
+template <int OP, typename A>
+__device__ __forceinline__ A scan_prefix_apply(A p, A q, A x, A* sp, A* sq) {
+    using R = ReconClamp<OP>;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // inclusive warp scan
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+        const A pp = __shfl_up_sync(0xffffffffu, p, off), pq = __shfl_up_sync(0xffffffffu, q, off);
+        if (lane >= off) {
+            // earlier lanes first: (p, q) <- (p, q) o (pp, pq)
+            A np = pp, nq = pq;
+            R::then(np, nq, p, q);
+            p = np;
+            q = nq;
+        }
+    }
+    if (lane == 31) {
+        sp[warp] = p;
+        sq[warp] = q;
+    }
+    __syncthreads();
+    if (warp == 0) {
+        A wp = sp[lane], wq = sq[lane];
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const A pp = __shfl_up_sync(0xffffffffu, wp, off), pq = __shfl_up_sync(0xffffffffu, wq, off);
+            if (lane >= off) {
+                A np = pp, nq = pq;
+                R::then(np, nq, wp, wq);
+                wp = np;
+                wq = nq;
+            }
+        }
+        sp[32 + lane] = wp;  // inclusive prefix over warps
+        sq[32 + lane] = wq;
+    }
+    __syncthreads();
+    // exclusive: the warps before this one, then the lanes before this one
+    if (warp > 0) x = R::apply(sp[32 + warp - 1], sq[32 + warp - 1], x);
+    const A lp = __shfl_up_sync(0xffffffffu, p, 1), lq = __shfl_up_sync(0xffffffffu, q, 1);
+    if (lane > 0) x = R::apply(lp, lq, x);
+    return x;
+}
+
+// One CTA per image row: left-to-right (when the SE has the left tap), then right-to-left (right tap),
+// in chunks of kScanChunk columns staged in shared memory.
+template <typename T, int OP>
+__global__ void __launch_bounds__(kScanThreads) recon_rows_kernel(T* __restrict__ y, const T* __restrict__ mask,
+                                                                  int W, int cls, int* __restrict__ flags) {
+    using A = typename Storage<T>::acc;
+    using R = ReconClamp<OP>;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    A* ys = reinterpret_cast<A*>(smem_raw);  // [kScanChunk], thread t's elements at t * kScanPer + k
+    A* ms = ys + kScanChunk;
+    __shared__ A sp[64], sq[64];
+    __shared__ A carry_s;
+    const long long row = blockIdx.x;
+    T* yr = y + row * W;
+    const T* mr = mask + row * W;
+    const int tid = threadIdx.x;
+    const A idp = Op<OP>::template neutral<A>();                                   // B's neutral
+    const A idq = Op<OP == kDilate ? kErode : kDilate>::template neutral<A>();     // C's neutral
+    const int chunks = (W + kScanChunk - 1) / kScanChunk;
+    bool changed = false;
+    for (int dir = 0; dir < 2; ++dir) {
+        if (!(cls & (dir == 0 ? kScanLeft : kScanRight))) continue;
+        A carry = idp;
+        for (int ci = 0; ci < chunks; ++ci) {
+            const int c0 = (dir == 0 ? ci : chunks - 1 - ci) * kScanChunk;
+            const int n = min(kScanChunk, W - c0);
+            const bool fresh = chunks > 1 || dir == 0 || !(cls & kScanLeft);
+            if (fresh) {
+                __syncthreads();
+                for (int i = tid; i < n; i += kScanThreads) {
+                    ys[i] = Storage<T>::load(yr[c0 + i]);
+                    ms[i] = Storage<T>::load(mr[c0 + i]);
+                }
+            }
+            __syncthreads();
+            // logical position l = tid * kScanPer + k runs along the scan direction
+            A p = idp, q = idq;
+#pragma unroll
+            for (int k = 0; k < kScanPer; ++k) {
+                const int l = tid * kScanPer + k;
+                if (l < n) {
+                    const int i = dir == 0 ? l : n - 1 - l;
+                    const A a = ys[i], m = ms[i];
+                    R::then(p, q, R::C(m, a), m);
+                }
+            }
+            A x = scan_prefix_apply<OP>(p, q, carry, sp, sq);
+#pragma unroll
+            for (int k = 0; k < kScanPer; ++k) {
+                const int l = tid * kScanPer + k;
+                if (l < n) {
+                    const int i = dir == 0 ? l : n - 1 - l;
+                    const A a = ys[i];
+                    const A v = R::apply(a, ms[i], x);
+                    if (!(v == a)) {
+                        changed = true;
+                        ys[i] = v;
+                    }
+                    x = v;
+                    if (l == n - 1) carry_s = v;
+                }
+            }
+            __syncthreads();
+            carry = carry_s;
+            const bool last = chunks > 1 || dir == 1 || !(cls & kScanRight);
+            if (last)
+                for (int i = tid; i < n; i += kScanThreads) yr[c0 + i] = Storage<T>::store(ys[i]);
+        }
+    }
+    if (__syncthreads_or(changed) && tid == 0) atomicOr(flags, 1);
+}
+
+// One CTA per 32-column strip of a plane; warp s holds rows [s * L, (s + 1) * L), lane j column j of
+// the strip.  Top-to-bottom (up tap), then bottom-to-top (down tap).  Each direction composes every
+// warp's run, scans the 32 runs of a column in order, and applies.  The top-to-bottom apply also
+// composes the bottom-to-top runs from the values it writes.
+template <typename T, int OP>
+__global__ void __launch_bounds__(kScanThreads) recon_cols_kernel(T* __restrict__ y, const T* __restrict__ mask,
+                                                                  int H, int W, int strips, int cls,
+                                                                  int* __restrict__ flags) {
+    using A = typename Storage<T>::acc;
+    using R = ReconClamp<OP>;
+    __shared__ A sp[32][kScanCols + 1], sq[32][kScanCols + 1];
+    const long long plane = blockIdx.x / strips;
+    const int strip = static_cast<int>(blockIdx.x % strips);
+    const int j = threadIdx.x & 31, s = threadIdx.x >> 5;
+    const int col = strip * kScanCols + j;
+    const bool ok = col < W;
+    const int L = (H + 31) / 32;
+    const int r0 = min(H, s * L), r1 = min(H, r0 + L);
+    T* yc = y + plane * H * W + col;
+    const T* mc = mask + plane * H * W + col;
+    const A idp = Op<OP>::template neutral<A>();
+    const A idq = Op<OP == kDilate ? kErode : kDilate>::template neutral<A>();
+    const bool down = cls & kScanUp, up = cls & kScanDown;
+    bool changed = false;
+
+    // exclusive prefix over the runs of this lane's column, in run order `order` (0: top first)
+    auto run_scan = [&](int order) {
+        __syncthreads();
+        if (s == 0) {
+            A p = idp, q = idq;
+            for (int t = 0; t < 32; ++t) {
+                const int r = order == 0 ? t : 31 - t;
+                const A fp = sp[r][j], fq = sq[r][j];
+                sp[r][j] = p;
+                sq[r][j] = q;
+                R::then(p, q, fp, fq);
+            }
+        }
+        __syncthreads();
+    };
+
+    if (down) {
+        A p = idp, q = idq;
+        if (ok)
+            for (int r = r0; r < r1; ++r) {
+                const A m = Storage<T>::load(mc[static_cast<long long>(r) * W]);
+                R::then(p, q, R::C(m, Storage<T>::load(yc[static_cast<long long>(r) * W])), m);
+            }
+        sp[s][j] = p;
+        sq[s][j] = q;
+        run_scan(0);
+        A x = R::apply(sp[s][j], sq[s][j], idp);
+        A bp = idp, bq = idq;  // bottom-to-top composition of this run, from the new values
+        if (ok)
+            for (int r = r0; r < r1; ++r) {
+                const long long o = static_cast<long long>(r) * W;
+                const A a = Storage<T>::load(yc[o]), m = Storage<T>::load(mc[o]);
+                const A v = R::apply(a, m, x);
+                if (!(v == a)) {
+                    changed = true;
+                    yc[o] = Storage<T>::store(v);
+                }
+                x = v;
+                if (up) {
+                    // prepend: the run's lower rows act first
+                    A np = R::C(m, v), nq = m;
+                    R::then(np, nq, bp, bq);
+                    bp = np;
+                    bq = nq;
+                }
+            }
+        __syncthreads();
+        sp[s][j] = bp;
+        sq[s][j] = bq;
+    } else if (up) {
+        A p = idp, q = idq;
+        if (ok)
+            for (int r = r1 - 1; r >= r0; --r) {
+                const A m = Storage<T>::load(mc[static_cast<long long>(r) * W]);
+                R::then(p, q, R::C(m, Storage<T>::load(yc[static_cast<long long>(r) * W])), m);
+            }
+        sp[s][j] = p;
+        sq[s][j] = q;
+    }
+    if (up) {
+        run_scan(1);
+        A x = R::apply(sp[s][j], sq[s][j], idp);
+        if (ok)
+            for (int r = r1 - 1; r >= r0; --r) {
+                const long long o = static_cast<long long>(r) * W;
+                const A a = Storage<T>::load(yc[o]), m = Storage<T>::load(mc[o]);
+                const A v = R::apply(a, m, x);
+                if (!(v == a)) {
+                    changed = true;
+                    yc[o] = Storage<T>::store(v);
+                }
+                x = v;
+            }
+    }
+    if (__syncthreads_or(changed) && threadIdx.x == 0) atomicOr(flags, 1);
+}
+
+}  // namespace serron

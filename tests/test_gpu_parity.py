@@ -233,17 +233,27 @@ def _se(kind: str, C: int, dtype: torch.dtype, g: torch.Generator) -> torch.Tens
         return torch.where(yy * yy + xx * xx <= 9, 0.0, float("-inf")).to(dtype)
     if kind == "flat1":
         return torch.zeros(1, 1, dtype=dtype)
+    if kind == "disk15":  # 31x31 flat disk: every row one span of zeros (wide kernel, shared cores)
+        yy, xx = torch.meshgrid(torch.arange(31) - 15, torch.arange(31) - 15, indexing="ij")
+        return torch.where(yy * yy + xx * xx <= 225, 0.0, float("-inf")).to(dtype)
+    if kind == "rand9x11":  # wide kernel, per-tap weights
+        return (torch.randn(9, 11, generator=g) * 0.1).to(dtype)
+    if kind == "ring9_neg0":  # rows with holes (walked tap by tap) and rows of -0.0 weights
+        w = torch.full((9, 13), -0.0)
+        w[3:6, 4:9] = float("-inf")
+        return w.to(dtype)
     raise KeyError(kind)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16, torch.float64])
-@pytest.mark.parametrize("kind", ["rand7_perch", "rand4x6", "flat15", "flat_5x17_perch", "disk3", "flat1"])
+@pytest.mark.parametrize("kind", ["rand7_perch", "rand4x6", "flat15", "flat_5x17_perch", "disk3", "flat1", "disk15",
+                                  "rand9x11", "ring9_neg0"])
 @pytest.mark.parametrize("border", [0, 1, 2])
 def test_oracle_parity_multi_tile(serron, dtype, kind, border):
     g = torch.Generator().manual_seed(hash((str(dtype), kind, border)) % (2**31))
     shape = (2, 3, 70, 133)
     x = torch.rand(*shape, generator=g).to(dtype)
-    if kind == "flat15":
+    if kind in ("flat15", "disk15", "ring9_neg0"):
         x = (x * 8).floor().to(dtype)  # many ties
     go = torch.randn(*shape, generator=g).to(dtype)
     w = _se(kind, shape[1], dtype, g)
