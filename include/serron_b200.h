@@ -181,7 +181,7 @@ SERRON_API int64_t serron_get_separable_min_k(int32_t device, int32_t dtype, int
  * the reference's Jacobi schedule and check_every test are reproduced, so the call fails exactly when
  * the reference would.  Synchronous (reads a convergence flag).  *steps receives the number of
  * scan rounds and relaxation launches, or Jacobi steps, taken.  Workspace:
- * serron_reconstruct_workspace_bytes (256 bytes of flags, then one byte per 64x64 tile for max_iter <= 0
+ * serron_reconstruct_workspace_bytes (256 bytes of flags, then two bytes per 64x64 tile for max_iter <= 0
  * or a second image for max_iter > 0).
  * --------------------------------------------------------------------------------------------- */
 SERRON_API int serron_reconstruct(int32_t dilate, const void* marker, const void* mask, const int64_t* sizes,

@@ -766,6 +766,7 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                     // changes nothing, that is the fixed point
                     const int cls = host_flags[2];
                     const int lines = cls & (kScanLeft | kScanRight | kScanUp | kScanDown);
+                    bool complete = false;  // the scans cover every tap of the full step
                     if ((cls & kScanFlat) && lines) {
                         using A = typename Storage<T>::acc;
                         const size_t row_smem = 2 * static_cast<size_t>(kScanChunk) * sizeof(A);
@@ -777,7 +778,7 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                         // side, which only the opposite scan covers
                         const bool lop = ((cls & kScanLeft) != 0) != ((cls & kScanRight) != 0);
                         const bool vop = ((cls & kScanUp) != 0) != ((cls & kScanDown) != 0);
-                        const bool complete = !(cls & kScanOther) && !(border == kReflect && (lop || vop));
+                        complete = !(cls & kScanOther) && !(border == kReflect && (lop || vop));
                         for (int round = 0; round < kScanRounds; ++round) {
                             SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
                             if (lines & (kScanLeft | kScanRight))
@@ -796,16 +797,29 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                             }
                         }
                     }
-                    // then tile relaxation to the fixed point; when a tile's halo reaches only its eight
-                    // neighbours, a launch runs only the tiles whose halo moved
-                    const bool worklist = kH < kRecTile && kW < kRecTile && H > kH && W > kW;
-                    uint8_t* dirty = worklist ? static_cast<uint8_t*>(tmp) : nullptr;
-                    if (dirty && !converged) SB_CUDA(cudaMemsetAsync(dirty, 1, blocks, stream));
+                    // then tile relaxation to the fixed point, over a worklist of tiles whose halo moved
+                    // (when a halo reaches only the eight neighbours): tiles solved by scans in shared
+                    // memory when the scans cover the SE, else by the full step
+                    const bool worklist = complete || (kH < kRecTile && kW < kRecTile && H > kH && W > kW);
+                    uint8_t* din = worklist ? static_cast<uint8_t*>(tmp) : nullptr;
+                    uint8_t* dout = worklist ? din + align256(blocks) : nullptr;
+                    const size_t scan_smem = scan_tile_smem<typename Storage<T>::acc>();
+                    if (complete) set_smem(recon_tile_scan_kernel<T, OP>, scan_smem);
+                    if (worklist && !converged) {
+                        SB_CUDA(cudaMemsetAsync(din, 1, blocks, stream));
+                        SB_CUDA(cudaMemsetAsync(dout, 0, blocks, stream));
+                    }
                     while (!converged) {
                         SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
-                        kernel_fn<<<grid_1d(blocks), kRecThreads, smem, stream>>>(
-                            static_cast<T*>(output), static_cast<const T*>(mask), static_cast<const T*>(kernel), C, H,
-                            W, kH, kW, kcs, static_cast<int>(border), tx, ty, 4 * kRecTile, flags, dirty);
+                        if (complete)
+                            recon_tile_scan_kernel<T, OP><<<grid_1d(blocks), 256, scan_smem, stream>>>(
+                                static_cast<T*>(output), static_cast<const T*>(mask), H, W, tx, ty, cls,
+                                4 * kRecTile, flags, din, dout);
+                        else
+                            kernel_fn<<<grid_1d(blocks), kRecThreads, smem, stream>>>(
+                                static_cast<T*>(output), static_cast<const T*>(mask), static_cast<const T*>(kernel),
+                                C, H, W, kH, kW, kcs, static_cast<int>(border), tx, ty, 4 * kRecTile, flags, din,
+                                dout);
                         SB_CUDA(cudaGetLastError());
                         ++taken;
                         SB_CUDA(cudaMemcpyAsync(host_flags, flags, sizeof(int), cudaMemcpyDeviceToHost, stream));
@@ -815,6 +829,10 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                             break;
                         }
                         SB_CHECK(taken < cap, name, ": relaxation did not settle");
+                        if (worklist) {
+                            std::swap(din, dout);
+                            SB_CUDA(cudaMemsetAsync(dout, 0, blocks, stream));
+                        }
                     }
                 } else {
                     // the reference's Jacobi schedule: check every `check_every` steps, stop at max_iter
@@ -1074,9 +1092,9 @@ int serron_reconstruct(int32_t dilate, const void* marker, const void* mask, con
 int64_t serron_reconstruct_workspace_bytes(const int64_t* sizes, int64_t dim, int32_t dtype, int64_t max_iter) {
     if (dim != 4 || sizes == nullptr || dtype < kF32 || dtype > kBF16) return -1;
     const int64_t total = sizes[0] * sizes[1] * sizes[2] * sizes[3];
-    // the Jacobi schedule's second buffer, or one dirty byte per relaxation tile
+    // the Jacobi schedule's second buffer, or two dirty bytes per relaxation tile (read / set)
     const int64_t tiles = sizes[0] * sizes[1] * ((sizes[2] + kRecTile - 1) / kRecTile) * ((sizes[3] + kRecTile - 1) / kRecTile);
-    return 256 + (max_iter > 0 ? align256(total * static_cast<int64_t>(elem_size(dtype))) : align256(tiles));
+    return 256 + (max_iter > 0 ? align256(total * static_cast<int64_t>(elem_size(dtype))) : 2 * align256(tiles));
 }
 
 }  // extern "C"

@@ -63,17 +63,19 @@ __global__ void recon_init_kernel(const T* __restrict__ marker, const T* __restr
     y[i] = Storage<T>::store(Clip<OP>::apply(a, m));
 }
 
-// With `dirty` (one byte per tile), a launch runs only the tiles flagged in it: a tile clears its flag
-// before reading, and a tile that changed flags its eight neighbours (after its writes are visible),
-// so a tile whose halo moved runs again in this launch or the next.  flags[0] is raised whenever a flag
-// is set; the host stops when a launch sets none.  Without `dirty` every tile runs and flags[0] says
-// whether anything changed.
+// With `dirty_in`, a launch runs only the tiles flagged in it, and a tile that changed flags its eight
+// neighbours (and itself, if its inner iterations ran out) in `dirty_out`.  Two arrays, swapped and
+// cleared by the host between launches: a tile that read a neighbour's halo while the neighbour was
+// still changing it is flagged for the next launch, which sees the neighbour's final writes.
+// flags[0] is raised whenever a flag is set; the host stops when a launch sets none.  Without
+// `dirty_in` every tile runs and flags[0] says whether anything changed.
 template <typename T, int OP>
 __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__ y, const T* __restrict__ mask,
                                                                  const T* __restrict__ w, int C, int H, int W, int kH,
                                                                  int kW, int kcs, int border, int tiles_x,
                                                                  int tiles_y, int max_inner, int* __restrict__ flags,
-                                                                 uint8_t* __restrict__ dirty) {
+                                                                 const uint8_t* __restrict__ dirty_in,
+                                                                 uint8_t* __restrict__ dirty_out) {
     using A = typename Storage<T>::acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int aH = kH / 2, aW = kW / 2;
@@ -93,18 +95,7 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
     const int tid = threadIdx.x;
     const A neutral = Op<OP>::template neutral<A>();
 
-    if (dirty) {
-        __shared__ int run;
-        if (tid == 0) {
-            run = dirty[b];
-            if (run) {
-                dirty[b] = 0;
-                __threadfence();
-            }
-        }
-        __syncthreads();
-        if (!run) return;
-    }
+    if (dirty_in && !dirty_in[b]) return;  // one byte, read alike by every thread
     for (int i = tid; i < kH * kW; i += kRecThreads) ws[i] = Storage<T>::load(wc[i]);
     for (int i = tid; i < sw * sh; i += kRecThreads) {
         const int r = i / sw, q = i - r * sw;
@@ -166,14 +157,12 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
             const int gr = h0 + lr, gq = w0 + lq;
             if (gr < H && gq < W) yp[static_cast<long long>(gr) * W + gq] = Storage<T>::store(ys[(lr + aH) * sw + lq + aW]);
         }
-        if (dirty) {
-            __threadfence();
-            __syncthreads();
+        if (dirty_in) {
             // the neighbours, and the tile itself when its inner iterations ran out before it settled
             if (tid < 9 && (tid != 4 || !settled)) {
                 const int nx = tx + tid % 3 - 1, ny = ty + tid / 3 - 1;
                 if (nx >= 0 && nx < tiles_x && ny >= 0 && ny < tiles_y)
-                    dirty[plane * tiles_x * tiles_y + static_cast<long long>(ny) * tiles_x + nx] = 1;
+                    dirty_out[plane * tiles_x * tiles_y + static_cast<long long>(ny) * tiles_x + nx] = 1;
             }
         }
         if (tid == 0) atomicOr(flags, 1);

@@ -301,4 +301,154 @@ __global__ void __launch_bounds__(kScanThreads) recon_cols_kernel(T* __restrict_
     if (__syncthreads_or(changed) && threadIdx.x == 0) atomicOr(flags, 1);
 }
 
+// Worklist tile for SEs the scans cover completely (flat, anchor plus some of the four direct
+// neighbours): a 64x64 tile with a one-pixel halo in shared memory, solved by repeated row and column
+// scans until none changes anything.  Four threads share a row (or a column), 16 pixels each: each
+// composes its run's clamps, the four runs are scanned with shuffles, then applied.  Halo cells outside
+// the image hold the neutral element (a border tap is left to the opposite scan, which reads the same
+// pixel).  A tile that changed a pixel on an edge flags the neighbour across that edge in
+// `dirty_out`; the launch runs the tiles flagged in `dirty_in` (recon_tile_kernel states why two).
+constexpr int kScanTile = 64;
+template <typename A>
+constexpr size_t scan_tile_smem() { return static_cast<size_t>((kScanTile + 2) + kScanTile) * (kScanTile + 3) * sizeof(A); }
+
+template <typename T, int OP>
+__global__ void __launch_bounds__(256) recon_tile_scan_kernel(T* __restrict__ y, const T* __restrict__ mask, int H,
+                                                              int W, int tiles_x, int tiles_y, int cls, int max_inner,
+                                                              int* __restrict__ flags,
+                                                              const uint8_t* __restrict__ dirty_in,
+                                                              uint8_t* __restrict__ dirty_out) {
+    using A = typename Storage<T>::acc;
+    using R = ReconClamp<OP>;
+    constexpr int TS = kScanTile, P = TS + 3;  // pitch: odd
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    A* ys = reinterpret_cast<A*>(smem_raw);  // [TS + 2][P], pixel (r, c) of the tile at (r + 1, c + 1)
+    A* ms = ys + (TS + 2) * P;                // [TS][P]
+    const long long b = blockIdx.x;
+    const int tx = static_cast<int>(b % tiles_x), ty = static_cast<int>((b / tiles_x) % tiles_y);
+    const long long plane = b / (static_cast<long long>(tiles_x) * tiles_y);
+    const int h0 = ty * TS, w0 = tx * TS;
+    T* yp = y + plane * H * W;
+    const T* mp = mask + plane * H * W;
+    const int tid = threadIdx.x;
+    const A idp = Op<OP>::template neutral<A>();
+    const A idq = Op<OP == kDilate ? kErode : kDilate>::template neutral<A>();
+
+    if (!dirty_in[b]) return;  // one byte, read alike by every thread
+    const int th = min(TS, H - h0), tw = min(TS, W - w0);
+    for (int i = tid; i < (TS + 2) * (TS + 2); i += 256) {
+        const int r = i / (TS + 2), q = i - r * (TS + 2);
+        const int gr = h0 + r - 1, gq = w0 + q - 1;
+        A v = idp;
+        if (gr >= 0 && gr < H && gq >= 0 && gq < W && r <= th + 1 && q <= tw + 1)
+            v = Storage<T>::load(yp[static_cast<long long>(gr) * W + gq]);
+        ys[r * P + q] = v;
+    }
+    for (int i = tid; i < TS * TS; i += 256) {
+        const int r = i / TS, q = i - r * TS;
+        ms[r * P + q] = (r < th && q < tw) ? Storage<T>::load(mp[static_cast<long long>(h0 + r) * W + w0 + q]) : idq;
+    }
+    __syncthreads();
+
+    // one line of n <= 64 cells, four runs of 16; `at(k)` is the k-th cell along the scan direction
+    // (a pointer into ys), `mk(k)` its mask, `x0` the cell before the first (halo)
+    const int line = tid >> 2, g = tid & 3;
+    // returns 1 when the first cell changed, 2 when the last did, 4 when any did
+    auto sweep = [&](auto at, auto mk, int n, A x0) {
+        const int k0 = g * 16, k1 = min(n, k0 + 16);
+        A p = idp, q = idq;
+        for (int k = k0; k < k1; ++k) R::then(p, q, R::C(mk(k), *at(k)), mk(k));
+#pragma unroll
+        for (int off = 1; off < 4; off <<= 1) {
+            const A pp = __shfl_up_sync(0xffffffffu, p, off, 4), pq = __shfl_up_sync(0xffffffffu, q, off, 4);
+            if (g >= off) {
+                A np = pp, nq = pq;
+                R::then(np, nq, p, q);
+                p = np;
+                q = nq;
+            }
+        }
+        const A lp = __shfl_up_sync(0xffffffffu, p, 1, 4), lq = __shfl_up_sync(0xffffffffu, q, 1, 4);
+        A x = g > 0 ? R::apply(lp, lq, x0) : x0;
+        int moved = 0;
+        for (int k = k0; k < k1; ++k) {
+            A* c = at(k);
+            const A v = R::apply(*c, mk(k), x);
+            if (!(v == *c)) {
+                *c = v;
+                moved |= 4 | (k == 0 ? 1 : 0) | (k == n - 1 ? 2 : 0);
+            }
+            x = v;
+        }
+        return moved;
+    };
+
+    bool any = false, settled = false;
+    int edges = 0;  // bit 0: top row changed, 1: bottom, 2: left column, 3: right
+    for (int it = 0; it < max_inner; ++it) {
+        int moved = 0;
+        const bool row_ok = line < th, col_ok = line < tw;
+        const int row_edges = (line == 0 ? 1 : 0) | (line == th - 1 ? 2 : 0);
+        const int col_edges = (line == 0 ? 4 : 0) | (line == tw - 1 ? 8 : 0);
+        if (cls & kScanLeft) {
+            const int m = sweep([&](int k) { return &ys[(line + 1) * P + k + 1]; },
+                                [&](int k) { return ms[line * P + k]; }, row_ok ? tw : 0,
+                                row_ok ? ys[(line + 1) * P] : idp);
+            if (m) edges |= row_edges | (m & 1 ? 4 : 0) | (m & 2 ? 8 : 0);
+            moved |= m;
+        }
+        if (cls & kScanRight) {
+            const int m = sweep([&](int k) { return &ys[(line + 1) * P + tw - k]; },
+                                [&](int k) { return ms[line * P + tw - 1 - k]; }, row_ok ? tw : 0,
+                                row_ok ? ys[(line + 1) * P + tw + 1] : idp);
+            if (m) edges |= row_edges | (m & 1 ? 8 : 0) | (m & 2 ? 4 : 0);
+            moved |= m;
+        }
+        __syncthreads();
+        if (cls & kScanUp) {
+            const int m = sweep([&](int k) { return &ys[(k + 1) * P + line + 1]; },
+                                [&](int k) { return ms[k * P + line]; }, col_ok ? th : 0, col_ok ? ys[line + 1] : idp);
+            if (m) edges |= col_edges | (m & 1 ? 1 : 0) | (m & 2 ? 2 : 0);
+            moved |= m;
+        }
+        if (cls & kScanDown) {
+            const int m = sweep([&](int k) { return &ys[(th - k) * P + line + 1]; },
+                                [&](int k) { return ms[(th - 1 - k) * P + line]; }, col_ok ? th : 0,
+                                col_ok ? ys[(th + 1) * P + line + 1] : idp);
+            if (m) edges |= col_edges | (m & 1 ? 2 : 0) | (m & 2 ? 1 : 0);
+            moved |= m;
+        }
+        if (!__syncthreads_or(moved)) {
+            settled = true;
+            break;
+        }
+        any = true;
+    }
+    if (!any) return;
+    for (int i = tid; i < th * tw; i += 256) {
+        const int r = i / tw, q = i - r * tw;
+        yp[static_cast<long long>(h0 + r) * W + w0 + q] = Storage<T>::store(ys[(r + 1) * P + q + 1]);
+    }
+    // the neighbours across the edges that moved, and the tile itself if it did not settle
+    __shared__ int edge_s;
+    if (tid == 0) edge_s = 0;
+    __syncthreads();
+    if (edges) atomicOr(&edge_s, edges);
+    __syncthreads();
+    if (tid < 5) {
+        const int e = edge_s;
+        int nx = tx, ny = ty;
+        bool go = false;
+        if (tid == 0) { ny = ty - 1; go = e & 1; }
+        if (tid == 1) { ny = ty + 1; go = e & 2; }
+        if (tid == 2) { nx = tx - 1; go = e & 4; }
+        if (tid == 3) { nx = tx + 1; go = e & 8; }
+        if (tid == 4) go = !settled;
+        if (go && nx >= 0 && nx < tiles_x && ny >= 0 && ny < tiles_y) {
+            dirty_out[plane * tiles_x * tiles_y + static_cast<long long>(ny) * tiles_x + nx] = 1;
+            atomicOr(flags, 1);
+        }
+    }
+}
+
 }  // namespace serron
