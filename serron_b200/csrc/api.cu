@@ -367,7 +367,10 @@ bool launch_forward_t(int algo, const Geometry& g, const void* x, const void* w,
             xp, wp, yp, ip, total, C, H, W, kH, kW, kcs, border);
     } else if (algo == kTiled) {
         const size_t acc = sizeof(typename Storage<T>::acc);
-        if (kW >= kWideQ + 1 && wide_smem(kH, kW, acc) <= kSmemOptin) {
+        // eight outputs per thread pay off from 9 columns, and from 5 for 16-bit storage (whose taps
+        // need no float-tie tracking, which costs the wide kernel registers)
+        const bool wide = kW >= kWideQ + 1 || (kW >= 5 && sizeof(T) == 2);
+        if (wide && wide_smem(kH, kW, acc) <= kSmemOptin) {
             const int tx = ceil_div(W, kWideCols), ty = ceil_div(H, kWideRows);
             const size_t smem = wide_smem(kH, kW, acc);
             auto kernel = wide_fwd_kernel<T, OP, I, V, X>;

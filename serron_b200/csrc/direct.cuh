@@ -244,7 +244,8 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
 }
 
 // ------------------------------------------------------------------------------------------------
-// wide tiled forward (algo = tiled, windows 9 or more columns wide): a 32x64 output tile, eight
+// wide tiled forward (algo = tiled, windows 9 or more columns wide, 5 or more for 16-bit storage):
+// a 32x64 output tile, eight
 // adjacent outputs per thread.  An SE row whose span holds one weight of zero (every row of a flat
 // disk, diamond or square) needs no per-tap weight: the eight windows over that row share the core
 // [c0 + lo + 7, c0 + hi], so the thread takes the core's first extremum once, suffix extrema of the
