@@ -815,7 +815,7 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                     while (!converged) {
                         SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
                         if (complete)
-                            recon_tile_scan_kernel<T, OP><<<grid_1d(blocks), 256, scan_smem, stream>>>(
+                            recon_tile_scan_kernel<T, OP><<<grid_1d(blocks), kScanTileThreads, scan_smem, stream>>>(
                                 static_cast<T*>(output), static_cast<const T*>(mask), H, W, tx, ty, cls,
                                 4 * kRecTile, flags, din, dout);
                         else

@@ -309,11 +309,13 @@ __global__ void __launch_bounds__(kScanThreads) recon_cols_kernel(T* __restrict_
 // pixel).  A tile that changed a pixel on an edge flags the neighbour across that edge in
 // `dirty_out`; the launch runs the tiles flagged in `dirty_in` (recon_tile_kernel states why two).
 constexpr int kScanTile = 64;
+constexpr int kScanTileThreads = 256;                           // four threads per line
+constexpr int kLineLanes = kScanTileThreads / kScanTile, kLineRun = kScanTile / kLineLanes;
 template <typename A>
 constexpr size_t scan_tile_smem() { return static_cast<size_t>((kScanTile + 2) + kScanTile) * (kScanTile + 3) * sizeof(A); }
 
 template <typename T, int OP>
-__global__ void __launch_bounds__(256) recon_tile_scan_kernel(T* __restrict__ y, const T* __restrict__ mask, int H,
+__global__ void __launch_bounds__(kScanTileThreads) recon_tile_scan_kernel(T* __restrict__ y, const T* __restrict__ mask, int H,
                                                               int W, int tiles_x, int tiles_y, int cls, int max_inner,
                                                               int* __restrict__ flags,
                                                               const uint8_t* __restrict__ dirty_in,
@@ -336,7 +338,7 @@ __global__ void __launch_bounds__(256) recon_tile_scan_kernel(T* __restrict__ y,
 
     if (!dirty_in[b]) return;  // one byte, read alike by every thread
     const int th = min(TS, H - h0), tw = min(TS, W - w0);
-    for (int i = tid; i < (TS + 2) * (TS + 2); i += 256) {
+    for (int i = tid; i < (TS + 2) * (TS + 2); i += kScanTileThreads) {
         const int r = i / (TS + 2), q = i - r * (TS + 2);
         const int gr = h0 + r - 1, gq = w0 + q - 1;
         A v = idp;
@@ -344,7 +346,7 @@ __global__ void __launch_bounds__(256) recon_tile_scan_kernel(T* __restrict__ y,
             v = Storage<T>::load(yp[static_cast<long long>(gr) * W + gq]);
         ys[r * P + q] = v;
     }
-    for (int i = tid; i < TS * TS; i += 256) {
+    for (int i = tid; i < TS * TS; i += kScanTileThreads) {
         const int r = i / TS, q = i - r * TS;
         ms[r * P + q] = (r < th && q < tw) ? Storage<T>::load(mp[static_cast<long long>(h0 + r) * W + w0 + q]) : idq;
     }
@@ -352,15 +354,18 @@ __global__ void __launch_bounds__(256) recon_tile_scan_kernel(T* __restrict__ y,
 
     // one line of n <= 64 cells, four runs of 16; `at(k)` is the k-th cell along the scan direction
     // (a pointer into ys), `mk(k)` its mask, `x0` the cell before the first (halo)
-    const int line = tid >> 2, g = tid & 3;
-    // returns 1 when the first cell changed, 2 when the last did, 4 when any did
-    auto sweep = [&](auto at, auto mk, int n, A x0) {
-        const int k0 = g * 16, k1 = min(n, k0 + 16);
+    const int line = tid / kLineLanes, g = tid % kLineLanes;
+    // returns 1 when the first cell changed, 2 when the last did, 4 when any did; `moved_at(k)` hears
+    // of every cell that changed
+    auto sweep = [&](auto at, auto mk, int n, A x0, auto moved_at) {
+        __syncwarp();  // the line's cells written by the other lanes in the previous sweep
+        const int k0 = g * kLineRun, k1 = min(n, k0 + kLineRun);
         A p = idp, q = idq;
         for (int k = k0; k < k1; ++k) R::then(p, q, R::C(mk(k), *at(k)), mk(k));
 #pragma unroll
-        for (int off = 1; off < 4; off <<= 1) {
-            const A pp = __shfl_up_sync(0xffffffffu, p, off, 4), pq = __shfl_up_sync(0xffffffffu, q, off, 4);
+        for (int off = 1; off < kLineLanes; off <<= 1) {
+            const A pp = __shfl_up_sync(0xffffffffu, p, off, kLineLanes);
+            const A pq = __shfl_up_sync(0xffffffffu, q, off, kLineLanes);
             if (g >= off) {
                 A np = pp, nq = pq;
                 R::then(np, nq, p, q);
@@ -368,7 +373,7 @@ __global__ void __launch_bounds__(256) recon_tile_scan_kernel(T* __restrict__ y,
                 q = nq;
             }
         }
-        const A lp = __shfl_up_sync(0xffffffffu, p, 1, 4), lq = __shfl_up_sync(0xffffffffu, q, 1, 4);
+        const A lp = __shfl_up_sync(0xffffffffu, p, 1, kLineLanes), lq = __shfl_up_sync(0xffffffffu, q, 1, kLineLanes);
         A x = g > 0 ? R::apply(lp, lq, x0) : x0;
         int moved = 0;
         for (int k = k0; k < k1; ++k) {
@@ -377,44 +382,63 @@ __global__ void __launch_bounds__(256) recon_tile_scan_kernel(T* __restrict__ y,
             if (!(v == *c)) {
                 *c = v;
                 moved |= 4 | (k == 0 ? 1 : 0) | (k == n - 1 ? 2 : 0);
+                moved_at(k);
             }
             x = v;
         }
         return moved;
     };
 
+    // lines to sweep: a row is swept again only after a column sweep moved one of its pixels, and a
+    // column only after a row sweep did (a line whose pixels did not move is still at its own fixed
+    // point, its halo ends being fixed during the launch)
+    __shared__ unsigned row_dirty[2], col_dirty[2];
+    if (tid < 2) {
+        row_dirty[tid] = ~0u;
+        col_dirty[tid] = ~0u;
+    }
+    __syncthreads();
     bool any = false, settled = false;
     int edges = 0;  // bit 0: top row changed, 1: bottom, 2: left column, 3: right
+    auto mark = [](unsigned* set, int i) { atomicOr(&set[i >> 5], 1u << (i & 31)); };
     for (int it = 0; it < max_inner; ++it) {
         int moved = 0;
-        const bool row_ok = line < th, col_ok = line < tw;
+        const bool rows_go = (row_dirty[line >> 5] >> (line & 31)) & 1u;
+        __syncthreads();
+        if (tid < 2) row_dirty[tid] = 0;
+        const bool row_ok = line < th && rows_go;
         const int row_edges = (line == 0 ? 1 : 0) | (line == th - 1 ? 2 : 0);
         const int col_edges = (line == 0 ? 4 : 0) | (line == tw - 1 ? 8 : 0);
         if (cls & kScanLeft) {
             const int m = sweep([&](int k) { return &ys[(line + 1) * P + k + 1]; },
                                 [&](int k) { return ms[line * P + k]; }, row_ok ? tw : 0,
-                                row_ok ? ys[(line + 1) * P] : idp);
+                                row_ok ? ys[(line + 1) * P] : idp, [&](int k) { mark(col_dirty, k); });
             if (m) edges |= row_edges | (m & 1 ? 4 : 0) | (m & 2 ? 8 : 0);
             moved |= m;
         }
         if (cls & kScanRight) {
             const int m = sweep([&](int k) { return &ys[(line + 1) * P + tw - k]; },
                                 [&](int k) { return ms[line * P + tw - 1 - k]; }, row_ok ? tw : 0,
-                                row_ok ? ys[(line + 1) * P + tw + 1] : idp);
+                                row_ok ? ys[(line + 1) * P + tw + 1] : idp, [&](int k) { mark(col_dirty, tw - 1 - k); });
             if (m) edges |= row_edges | (m & 1 ? 8 : 0) | (m & 2 ? 4 : 0);
             moved |= m;
         }
         __syncthreads();
+        const bool cols_go = (col_dirty[line >> 5] >> (line & 31)) & 1u;
+        __syncthreads();
+        if (tid < 2) col_dirty[tid] = 0;
+        const bool col_ok = line < tw && cols_go;
         if (cls & kScanUp) {
             const int m = sweep([&](int k) { return &ys[(k + 1) * P + line + 1]; },
-                                [&](int k) { return ms[k * P + line]; }, col_ok ? th : 0, col_ok ? ys[line + 1] : idp);
+                                [&](int k) { return ms[k * P + line]; }, col_ok ? th : 0, col_ok ? ys[line + 1] : idp,
+                                [&](int k) { mark(row_dirty, k); });
             if (m) edges |= col_edges | (m & 1 ? 1 : 0) | (m & 2 ? 2 : 0);
             moved |= m;
         }
         if (cls & kScanDown) {
             const int m = sweep([&](int k) { return &ys[(th - k) * P + line + 1]; },
                                 [&](int k) { return ms[(th - 1 - k) * P + line]; }, col_ok ? th : 0,
-                                col_ok ? ys[(th + 1) * P + line + 1] : idp);
+                                col_ok ? ys[(th + 1) * P + line + 1] : idp, [&](int k) { mark(row_dirty, th - 1 - k); });
             if (m) edges |= col_edges | (m & 1 ? 2 : 0) | (m & 2 ? 1 : 0);
             moved |= m;
         }
@@ -425,7 +449,7 @@ __global__ void __launch_bounds__(256) recon_tile_scan_kernel(T* __restrict__ y,
         any = true;
     }
     if (!any) return;
-    for (int i = tid; i < th * tw; i += 256) {
+    for (int i = tid; i < th * tw; i += kScanTileThreads) {
         const int r = i / tw, q = i - r * tw;
         yp[static_cast<long long>(h0 + r) * W + w0 + q] = Storage<T>::store(ys[(r + 1) * P + q + 1]);
     }
