@@ -41,7 +41,9 @@ struct SweepGeom {
     static constexpr int RR = TH + K - 1;                // row-result rows: K-1 carried + TH new
     static constexpr int NCC = TH / K;                   // column-pass chunks per column
     static constexpr size_t XS_BYTES = ((size_t(TH) * XS * ELEM + 15) / 16) * 16;
-    static constexpr size_t fwd_smem() { return 2 * XS_BYTES + size_t(RR) * RS * 4 + size_t(RR) * RS; }
+    static constexpr size_t RD_END = ((2 * XS_BYTES + size_t(RR) * RS * 4 + size_t(RR) * RS) + 15) / 16 * 16;
+    static constexpr int QCAP = 32 * K;  // winner-cell queue of a warp: one task's pushes at most
+    static constexpr size_t fwd_smem() { return RD_END + size_t(kSweepThreads / 32) * QCAP * 2; }
 };
 
 // One run of K windows [m, m+K-1], m = 0..K-1, over samples v[0..2K-2]: value and first-extremum
@@ -84,14 +86,16 @@ __device__ __forceinline__ float load_clean(T v, float neutral) {
 }
 
 // With `map` (records only), every winner is also set in the target map of the gather (one bit per
-// pixel, rows of ceil(W / 32) words, zero on entry): an output flags the row result its winner lies in
-// (bit 7 of that result's dj byte), and after the step each flagged result ORs its pixel into the map.
+// pixel, rows of ceil(W / 32) words, zero on entry).  In the column pass a lane whose winning row
+// result differs from the one of the output above pushes it to its warp's queue (ballot + popc: only
+// the few changes take a slot); the warp then decodes its queue densely into winner pixels and ORs
+// each into the map, skipping one equal to its queue neighbour's.
 template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX, int K>
 __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                                       I* __restrict__ win, uint32_t* __restrict__ map,
                                                                       int H, int W, int border, int strips, int segs,
                                                                       int seg_h) {
-    static_assert(K <= 128, "dj and its flag share a byte");
+    static_assert(K <= 255, "dj is a byte");
     using G = SweepGeom<K, sizeof(T)>;
     constexpr int a = G::a, TH = G::TH, Cc = G::Cc, XS = G::XS, RS = G::RS;
     constexpr bool ASYNC = sizeof(T) == 4;
@@ -100,6 +104,7 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
     T* const xsb1 = reinterpret_cast<T*>(smem_raw + G::XS_BYTES);
     float* rv = reinterpret_cast<float*>(smem_raw + 2 * G::XS_BYTES);   // [RR][RS]
     uint8_t* rdj = reinterpret_cast<uint8_t*>(rv + G::RR * RS);         // [RR][RS]
+    uint16_t* const queue = reinterpret_cast<uint16_t*>(smem_raw + G::RD_END) + (threadIdx.x >> 5) * G::QCAP;
 
     const long long b = blockIdx.x;
     const int strip = static_cast<int>(b % strips);
@@ -217,47 +222,48 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
             const int o0 = (s0 + base) * W + ow;
             T* yp = y + plane * H * W;
             I* wp = win + plane * H * W;
-            uint8_t* dj_col = rdj + base * RS + j;
+            const uint8_t* dj_col = rdj + base * RS + j;
+            int qn = 0, prev = -1;  // queue length (warp-uniform), this lane's last pushed row result
             sweep_run<K, OP, WITH_INDEX>(v, [&](int m, float val, int off) {
                 const bool out_ok = col_ok && base + m < rows_left;
                 const int o = o0 + m * W;
                 if (WITH_VALUE && out_ok) yp[o] = Storage<T>::store(val);
                 if (WITH_INDEX && out_ok) {
-                    // winning row base + m + off, and the column its own row pass chose (bit 7: flagged)
+                    // winning row base + m + off, and the column its own row pass chose
                     const uint32_t djb = dj_col[(m + off) * RS];
-                    const uint32_t t =
-                        val == neutral ? IndexTraits<I>::none : static_cast<uint32_t>(off * K) + (djb & 0x7fu);
-                    wp[o] = static_cast<I>(t);
-                    // every writer of the flag writes the same byte
-                    if (marking && val != neutral) dj_col[(m + off) * RS] = static_cast<uint8_t>(djb | 0x80u);
+                    wp[o] = static_cast<I>(val == neutral ? IndexTraits<I>::none : static_cast<uint32_t>(off * K) + djb);
+                }
+                if (marking) {
+                    const int cell = out_ok && val != neutral ? base + m + off : -1;
+                    const bool push = cell >= 0 && cell != prev;
+                    prev = cell;
+                    const unsigned bal = __ballot_sync(0xffffffffu, push);
+                    if (push) queue[qn + __popc(bal & ((1u << lane) - 1u))] = static_cast<uint16_t>(cell * kSweepTW + j);
+                    qn += __popc(bal);
                 }
             });
+            if (marking) {
+                // the queued row results' winners (row s0 - a + i, column ow0 + j - a + dj, border folded)
+                __syncwarp();
+                for (int q0 = 0; q0 < qn; q0 += 32) {
+                    int key = -1, wx = 0, wy = 0;
+                    if (q0 + lane < qn) {
+                        const int e = queue[q0 + lane];
+                        const int i = e / kSweepTW, jj = e - i * kSweepTW;
+                        wx = s0 - a + i;
+                        wy = ow0 + jj - a + static_cast<int>(rdj[i * RS + jj]);
+                        if ((static_cast<unsigned>(wx) < static_cast<unsigned>(H) || resolve(wx, H, border)) &&
+                            (static_cast<unsigned>(wy) < static_cast<unsigned>(W) || resolve(wy, W, border)))
+                            key = wx * W + wy;  // < H * W < 2^31
+                    }
+                    const int left = __shfl_up_sync(0xffffffffu, key, 1);
+                    if (key >= 0 && (lane == 0 || left != key))
+                        atomicOr(&map[(plane * H + wx) * WW + (wy >> 5)], 1u << (wy & 31));
+                }
+                __syncwarp();  // the queue is refilled by the warp's next task
+            }
         }
         __syncthreads();
-        // flagged row results give the step's winners (row s0 - a + i, column ow0 + j - a + dj, border
-        // folded) to the target map; a lane skips the OR when its left neighbour, which usually has the same
-        // winner, does it.  Flags are cleared for the carry.  RR * 64 is a multiple of 32: warps run whole.
-        if (marking) {
-            for (int c = tid; c < G::RR * kSweepTW; c += kSweepThreads) {
-                const int i = c / kSweepTW, j = c - i * kSweepTW;
-                uint8_t* cell = rdj + i * RS + j;
-                const uint32_t d = *cell;
-                int wx = -1, wy = 0;
-                if (d & 0x80u) {
-                    *cell = static_cast<uint8_t>(d & 0x7fu);
-                    wx = s0 - a + i;
-                    wy = ow0 + j - a + static_cast<int>(d & 0x7fu);
-                    if (!((static_cast<unsigned>(wx) < static_cast<unsigned>(H) || resolve(wx, H, border)) &&
-                          (static_cast<unsigned>(wy) < static_cast<unsigned>(W) || resolve(wy, W, border))))
-                        wx = -1;
-                }
-                const int key = wx < 0 ? -1 : wx * W + wy;  // < H * W < 2^31
-                const int left = __shfl_up_sync(0xffffffffu, key, 1);
-                if (key >= 0 && (lane == 0 || left != key))
-                    atomicOr(&map[(plane * H + wx) * WW + (wy >> 5)], 1u << (wy & 31));
-            }
-            __syncthreads();
-        }
         // carry the last K-1 row results to the top
         for (int i = tid; i < (K - 1) * RS; i += kSweepThreads) {
             rv[i] = rv[TH * RS + i];
