@@ -782,7 +782,11 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                         const bool lop = ((cls & kScanLeft) != 0) != ((cls & kScanRight) != 0);
                         const bool vop = ((cls & kScanUp) != 0) != ((cls & kScanDown) != 0);
                         complete = !(cls & kScanOther) && !(border == kReflect && (lop || vop));
-                        for (int round = 0; round < kScanRounds; ++round) {
+                        // the shared-memory scan tiles alone do best when they cover the SE (measured on the
+                        // 8192^2 blob mask: 176 ms with no global round, 208 ms with 8); the full-step tiles
+                        // need the global rounds to carry the fronts
+                        const int rounds = complete ? 0 : kScanRounds;
+                        for (int round = 0; round < rounds; ++round) {
                             SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
                             if (lines & (kScanLeft | kScanRight))
                                 rows_fn<<<grid_1d(rows), kScanThreads, row_smem, stream>>>(

@@ -13,8 +13,8 @@
 // `recon_cols_kernel` runs top-to-bottom then bottom-to-top over 32-column strips, each warp holding
 // one run of rows.  A round of both carries a front across the image along any path that turns a
 // few times, where the tile relaxation moves it one tile per launch.  The host runs a few such rounds
-// and leaves the rest (paths that turn often, taps the scans do not cover) to recon_tile_kernel,
-// which also confirms the fixed point.
+// ahead of recon_tile_kernel (SEs with taps the scans do not cover), which also confirms the fixed
+// point; SEs the scans cover go straight to the worklist of recon_tile_scan_kernel below.
 //
 // Border taps are skipped by the scans (a partial update is still a valid one); where that leaves a
 // tap of the full step uncovered (REFLECT with a one-sided line tap, whose edge sample lies on the
@@ -30,7 +30,7 @@ constexpr int kScanThreads = 1024;
 constexpr int kScanPer = 8;                          // elements per thread in a row chunk
 constexpr int kScanChunk = kScanThreads * kScanPer;  // row chunk held in shared memory
 constexpr int kScanCols = 32;                        // columns per CTA of the column scan
-constexpr int kScanRounds = 8;                       // scan rounds before the tile relaxation takes over
+constexpr int kScanRounds = 8;                       // global scan rounds before full-step tile relaxation
 
 // SE classes found on the device (bits of flags[2])
 constexpr int kScanFlat = 1;     // every present tap has weight 0 and the anchor is present
