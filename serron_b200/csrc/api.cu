@@ -770,7 +770,8 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                     const int cls = host_flags[2];
                     const int lines = cls & (kScanLeft | kScanRight | kScanUp | kScanDown);
                     bool complete = false;  // the scans cover every tap of the full step
-                    if ((cls & kScanFlat) && lines) {
+                    const int diags = cls & kScanDiag;
+                    if ((cls & kScanFlat) && (lines || diags)) {
                         using A = typename Storage<T>::acc;
                         const size_t row_smem = 2 * static_cast<size_t>(kScanChunk) * sizeof(A);
                         auto rows_fn = recon_rows_kernel<T, OP>;
@@ -781,12 +782,16 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                         // side, which only the opposite scan covers
                         const bool lop = ((cls & kScanLeft) != 0) != ((cls & kScanRight) != 0);
                         const bool vop = ((cls & kScanUp) != 0) != ((cls & kScanDown) != 0);
-                        complete = !(cls & kScanOther) && !(border == kReflect && (lop || vop));
+                        // a folded diagonal tap lands on another tap of the 3x3 neighbourhood, which only
+                        // the full square is sure to hold
+                        const bool square = lines == (kScanLeft | kScanRight | kScanUp | kScanDown) && diags == kScanDiag;
+                        complete = !(cls & kScanOther) &&
+                                   (diags ? border == kConstant || square : !(border == kReflect && (lop || vop)));
                         // the shared-memory scan tiles alone do best when they cover the SE (measured on the
                         // 8192^2 blob mask: 176 ms with no global round, 208 ms with 8); the full-step tiles
                         // need the global rounds to carry the fronts
                         const int rounds = complete ? 0 : kScanRounds;
-                        for (int round = 0; round < rounds; ++round) {
+                        for (int round = 0; round < (lines ? rounds : 0); ++round) {
                             SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
                             if (lines & (kScanLeft | kScanRight))
                                 rows_fn<<<grid_1d(rows), kScanThreads, row_smem, stream>>>(

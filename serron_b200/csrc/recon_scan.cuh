@@ -38,7 +38,12 @@ constexpr int kScanLeft = 2;     // tap sampling (row, column - 1)
 constexpr int kScanRight = 4;    // (row, column + 1)
 constexpr int kScanUp = 8;       // (row - 1, column)
 constexpr int kScanDown = 16;    // (row + 1, column)
-constexpr int kScanOther = 32;   // any other present tap
+constexpr int kScanOther = 32;   // a present tap outside the 3x3 neighbourhood
+constexpr int kScanUL = 64;      // (row - 1, column - 1)
+constexpr int kScanUR = 128;     // (row - 1, column + 1)
+constexpr int kScanDL = 256;     // (row + 1, column - 1)
+constexpr int kScanDR = 512;     // (row + 1, column + 1)
+constexpr int kScanDiag = kScanUL | kScanUR | kScanDL | kScanDR;
 
 // one step of the reconstruction as a clamp: f(x) = C(q, B(p, x))
 template <int OP>
@@ -76,6 +81,10 @@ __global__ void recon_se_class_kernel(const T* __restrict__ w, int kH, int kW, i
             else if (dr == 0 && dc == 1) cls |= kScanRight;
             else if (dr == -1 && dc == 0) cls |= kScanUp;
             else if (dr == 1 && dc == 0) cls |= kScanDown;
+            else if (dr == -1 && dc == -1) cls |= kScanUL;
+            else if (dr == -1 && dc == 1) cls |= kScanUR;
+            else if (dr == 1 && dc == -1) cls |= kScanDL;
+            else if (dr == 1 && dc == 1) cls |= kScanDR;
             else cls |= kScanOther;
         }
     if (flat && anchor) cls |= kScanFlat;
@@ -301,9 +310,9 @@ __global__ void __launch_bounds__(kScanThreads) recon_cols_kernel(T* __restrict_
     if (__syncthreads_or(changed) && threadIdx.x == 0) atomicOr(flags, 1);
 }
 
-// Worklist tile for SEs the scans cover completely (flat, anchor plus some of the four direct
-// neighbours): a 64x64 tile with a one-pixel halo in shared memory, solved by repeated row and column
-// scans until none changes anything.  Four threads share a row (or a column), 16 pixels each: each
+// Worklist tile for flat SEs within the 3x3 neighbourhood (anchor plus any of the eight neighbours):
+// a 64x64 tile with a one-pixel halo in shared memory, solved by repeated row and column scans (the
+// four line taps) and an in-place pass of the diagonal taps, until none changes anything.  Four threads share a row (or a column), 16 pixels each: each
 // composes its run's clamps, the four runs are scanned with shuffles, then applied.  Halo cells outside
 // the image hold the neutral element (a border tap is left to the opposite scan, which reads the same
 // pixel).  A tile that changed a pixel on an edge flags the neighbour across that edge in
@@ -409,18 +418,23 @@ __global__ void __launch_bounds__(kScanTileThreads) recon_tile_scan_kernel(T* __
         const bool row_ok = line < th && rows_go;
         const int row_edges = (line == 0 ? 1 : 0) | (line == th - 1 ? 2 : 0);
         const int col_edges = (line == 0 ? 4 : 0) | (line == tw - 1 ? 8 : 0);
+        // corner bits (read by diagonal neighbours): 16 top-left, 32 top-right, 64 bottom-left, 128 bottom-right
+        const int left_c = (line == 0 ? 16 : 0) | (line == th - 1 ? 64 : 0);   // row `line`, column 0
+        const int right_c = (line == 0 ? 32 : 0) | (line == th - 1 ? 128 : 0); // row `line`, last column
+        const int top_c = (line == 0 ? 16 : 0) | (line == tw - 1 ? 32 : 0);    // column `line`, row 0
+        const int bot_c = (line == 0 ? 64 : 0) | (line == tw - 1 ? 128 : 0);   // column `line`, last row
         if (cls & kScanLeft) {
             const int m = sweep([&](int k) { return &ys[(line + 1) * P + k + 1]; },
                                 [&](int k) { return ms[line * P + k]; }, row_ok ? tw : 0,
                                 row_ok ? ys[(line + 1) * P] : idp, [&](int k) { mark(col_dirty, k); });
-            if (m) edges |= row_edges | (m & 1 ? 4 : 0) | (m & 2 ? 8 : 0);
+            if (m) edges |= row_edges | (m & 1 ? 4 | left_c : 0) | (m & 2 ? 8 | right_c : 0);
             moved |= m;
         }
         if (cls & kScanRight) {
             const int m = sweep([&](int k) { return &ys[(line + 1) * P + tw - k]; },
                                 [&](int k) { return ms[line * P + tw - 1 - k]; }, row_ok ? tw : 0,
                                 row_ok ? ys[(line + 1) * P + tw + 1] : idp, [&](int k) { mark(col_dirty, tw - 1 - k); });
-            if (m) edges |= row_edges | (m & 1 ? 8 : 0) | (m & 2 ? 4 : 0);
+            if (m) edges |= row_edges | (m & 1 ? 8 | right_c : 0) | (m & 2 ? 4 | left_c : 0);
             moved |= m;
         }
         __syncthreads();
@@ -432,15 +446,40 @@ __global__ void __launch_bounds__(kScanTileThreads) recon_tile_scan_kernel(T* __
             const int m = sweep([&](int k) { return &ys[(k + 1) * P + line + 1]; },
                                 [&](int k) { return ms[k * P + line]; }, col_ok ? th : 0, col_ok ? ys[line + 1] : idp,
                                 [&](int k) { mark(row_dirty, k); });
-            if (m) edges |= col_edges | (m & 1 ? 1 : 0) | (m & 2 ? 2 : 0);
+            if (m) edges |= col_edges | (m & 1 ? 1 | top_c : 0) | (m & 2 ? 2 | bot_c : 0);
             moved |= m;
         }
         if (cls & kScanDown) {
             const int m = sweep([&](int k) { return &ys[(th - k) * P + line + 1]; },
                                 [&](int k) { return ms[(th - 1 - k) * P + line]; }, col_ok ? th : 0,
                                 col_ok ? ys[(th + 1) * P + line + 1] : idp, [&](int k) { mark(row_dirty, th - 1 - k); });
-            if (m) edges |= col_edges | (m & 1 ? 2 : 0) | (m & 2 ? 1 : 0);
+            if (m) edges |= col_edges | (m & 1 ? 2 | bot_c : 0) | (m & 2 ? 1 | top_c : 0);
             moved |= m;
+        }
+        if (cls & kScanDiag) {
+            // the diagonal taps, in place (a neighbour read before or after its own update is a value the
+            // step could give: either way the update is a valid one)
+            __syncthreads();
+            for (int i = tid; i < th * tw; i += kScanTileThreads) {
+                const int r = i / tw, c = i - r * tw;
+                A* cell = &ys[(r + 1) * P + c + 1];
+                A x = idp;
+                if (cls & kScanUL) x = R::B(x, cell[-P - 1]);
+                if (cls & kScanUR) x = R::B(x, cell[-P + 1]);
+                if (cls & kScanDL) x = R::B(x, cell[P - 1]);
+                if (cls & kScanDR) x = R::B(x, cell[P + 1]);
+                const A a0 = *cell;
+                const A v = R::apply(a0, ms[r * P + c], x);
+                if (!(v == a0)) {
+                    *cell = v;
+                    mark(row_dirty, r);
+                    mark(col_dirty, c);
+                    moved |= 4;
+                    edges |= (r == 0 ? 1 : 0) | (r == th - 1 ? 2 : 0) | (c == 0 ? 4 : 0) | (c == tw - 1 ? 8 : 0);
+                    edges |= (r == 0 && c == 0 ? 16 : 0) | (r == 0 && c == tw - 1 ? 32 : 0) |
+                             (r == th - 1 && c == 0 ? 64 : 0) | (r == th - 1 && c == tw - 1 ? 128 : 0);
+                }
+            }
         }
         if (!__syncthreads_or(moved)) {
             settled = true;
@@ -453,14 +492,16 @@ __global__ void __launch_bounds__(kScanTileThreads) recon_tile_scan_kernel(T* __
         const int r = i / tw, q = i - r * tw;
         yp[static_cast<long long>(h0 + r) * W + w0 + q] = Storage<T>::store(ys[(r + 1) * P + q + 1]);
     }
-    // the neighbours across the edges that moved, and the tile itself if it did not settle
+    // the neighbours across the edges (and, with diagonal taps, corners) that moved, and the tile itself
+    // if it did not settle
     __shared__ int edge_s;
     if (tid == 0) edge_s = 0;
     __syncthreads();
     if (edges) atomicOr(&edge_s, edges);
     __syncthreads();
-    if (tid < 5) {
+    if (tid < 9) {
         const int e = edge_s;
+        const bool diag = cls & kScanDiag;
         int nx = tx, ny = ty;
         bool go = false;
         if (tid == 0) { ny = ty - 1; go = e & 1; }
@@ -468,6 +509,10 @@ __global__ void __launch_bounds__(kScanTileThreads) recon_tile_scan_kernel(T* __
         if (tid == 2) { nx = tx - 1; go = e & 4; }
         if (tid == 3) { nx = tx + 1; go = e & 8; }
         if (tid == 4) go = !settled;
+        if (tid == 5) { nx = tx - 1; ny = ty - 1; go = diag && (e & 16); }
+        if (tid == 6) { nx = tx + 1; ny = ty - 1; go = diag && (e & 32); }
+        if (tid == 7) { nx = tx - 1; ny = ty + 1; go = diag && (e & 64); }
+        if (tid == 8) { nx = tx + 1; ny = ty + 1; go = diag && (e & 128); }
         if (go && nx >= 0 && nx < tiles_x && ny >= 0 && ny < tiles_y) {
             dirty_out[plane * tiles_x * tiles_y + static_cast<long long>(ny) * tiles_x + nx] = 1;
             atomicOr(flags, 1);

@@ -1,10 +1,10 @@
 """Reconstruction to convergence (max_iter=None) on the directional-scan path against the reference's
 own Jacobi schedule (max_iter set, recon_step_kernel) and against the oracle.
 
-Flat structuring elements with an anchor and a direct neighbour take row and column scans, then the
-worklist tile relaxation; the result must equal the Jacobi fixed point bit for bit on every dtype,
-border and shape, including rows longer than one scan chunk (8192 columns), columns split unevenly
-into runs, single rows and single columns.
+Flat structuring elements within the 3x3 neighbourhood take the worklist of scan tiles (row and column
+scans plus a diagonal pass), others the full-step tiles after global scan rounds; the result must
+equal the Jacobi fixed point bit for bit on every dtype, border and shape, including rows longer than
+one scan chunk (8192 columns), columns split unevenly into runs, single rows and single columns.
 """
 
 from __future__ import annotations
@@ -43,6 +43,10 @@ def _se(kind: str, dtype) -> torch.Tensor:
         w = [[0, 0, NINF]]
     elif kind == "down2":  # anchor and lower neighbour only
         w = [[NINF], [0], [0]]
+    elif kind == "x3":  # anchor and the four diagonals (the diagonal pass alone)
+        w = [[0, NINF, 0], [NINF, 0, NINF], [0, NINF, 0]]
+    elif kind == "diag2":  # anchor, upper-left and lower-right: folds need taps it lacks except under CONSTANT
+        w = [[0, NINF, NINF], [NINF, 0, NINF], [NINF, NINF, 0]]
     elif kind == "nonflat3":  # weights: the tile relaxation alone
         w = [[NINF, -0.25, NINF], [-0.25, 0, -0.25], [NINF, -0.25, NINF]]
     else:
@@ -81,7 +85,8 @@ SHAPES = [(2, 3, 37, 61), (1, 1, 33, 8200), (1, 2, 200, 40), (1, 1, 1, 70), (1, 
 
 
 @pytest.mark.parametrize("shape", SHAPES, ids=lambda s: "x".join(map(str, s)))
-@pytest.mark.parametrize("kind", ["cross3", "square3", "hline3", "vline3", "hline5", "left2", "down2", "nonflat3"])
+@pytest.mark.parametrize("kind", ["cross3", "square3", "hline3", "vline3", "hline5", "left2", "down2", "x3", "diag2",
+                                  "nonflat3"])
 def test_scan_path_equals_jacobi_fixed_point(serron, shape, kind):
     gen = torch.Generator().manual_seed(zlib.crc32(repr((shape, kind)).encode()))
     mask = _smooth_mask(shape, gen)
@@ -95,7 +100,7 @@ def test_scan_path_equals_jacobi_fixed_point(serron, shape, kind):
                 assert torch.equal(got, want), (kind, dtype, border, dilate)
 
 
-@pytest.mark.parametrize("kind", ["cross3", "square3", "hline5", "nonflat3"])
+@pytest.mark.parametrize("kind", ["cross3", "square3", "hline5", "x3", "nonflat3"])
 def test_scan_path_equals_oracle(serron, kind):
     gen = torch.Generator().manual_seed(11)
     shape = (1, 2, 23, 29)
