@@ -261,8 +261,13 @@ int format_bytes(int fmt) {
 }
 bool format_is_separable(int fmt) { return base_format(fmt) >= SERRON_WINNERS_SEPARABLE_U8; }
 
+// the tile with its halo and weights, then the target-map bitmap of the halo
 size_t tiled_smem_bytes(int64_t kH, int64_t kW, int dtype) {
-    return tiled_smem(static_cast<int>(kH), static_cast<int>(kW), acc_size(dtype));
+    const int h = static_cast<int>(kH), w = static_cast<int>(kW);
+    return (tiled_smem(h, w, acc_size(dtype)) + 15) / 16 * 16 + mark_bytes(kTile, kTile, h, w);
+}
+size_t wide_smem_bytes(int kH, int kW, size_t acc) {
+    return (wide_smem(kH, kW, acc) + 15) / 16 * 16 + mark_bytes(kWideRows, kWideCols, kH, kW);
 }
 size_t sep_smem_bytes(int64_t kH, int64_t kW, int dtype) {
     return dtype == kF64 ? SepSmem<double>::bytes(static_cast<int>(kH), static_cast<int>(kW))
@@ -351,7 +356,8 @@ unsigned int grid_1d(long long blocks) {
 // ------------------------------------------------------------------------------------------------
 // launches
 // ------------------------------------------------------------------------------------------------
-// Returns true when the launch also filled `map` (the separable sweep does, for its window lengths).
+// Returns true when the launch also filled `map` (the separable sweep, for its window lengths, and the
+// tiled kernels do).
 template <typename T, int OP, typename I, bool V, bool X>
 bool launch_forward_t(int algo, const Geometry& g, const void* x, const void* w, void* y, void* win, uint32_t* map,
                       int border, cudaStream_t stream) {
@@ -370,21 +376,24 @@ bool launch_forward_t(int algo, const Geometry& g, const void* x, const void* w,
         // eight outputs per thread pay off from 9 columns, and from 5 for 16-bit storage (whose taps
         // need no float-tie tracking, which costs the wide kernel registers)
         const bool wide = kW >= kWideQ + 1 || (kW >= 5 && sizeof(T) == 2);
-        if (wide && wide_smem(kH, kW, acc) <= kSmemOptin) {
+        uint32_t* marks = X ? map : nullptr;
+        if (wide && wide_smem_bytes(kH, kW, acc) <= kSmemOptin) {
             const int tx = ceil_div(W, kWideCols), ty = ceil_div(H, kWideRows);
-            const size_t smem = wide_smem(kH, kW, acc);
+            const size_t smem = wide_smem_bytes(kH, kW, acc);
             auto kernel = wide_fwd_kernel<T, OP, I, V, X>;
             set_smem(kernel, smem);
             kernel<<<grid_1d(static_cast<long long>(tx) * ty * g.N * g.C), 256, smem, stream>>>(
-                xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty);
+                xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty, marks);
         } else {
             const int tx = ceil_div(W, kTile), ty = ceil_div(H, kTile);
             const size_t smem = tiled_smem_bytes(kH, kW, std::is_same<T, double>::value ? kF64 : kF32);
             auto kernel = tiled_fwd_kernel<T, OP, I, V, X>;
             set_smem(kernel, smem);
             kernel<<<grid_1d(static_cast<long long>(tx) * ty * g.N * g.C), dim3(kTile, kTileThreadsY), smem, stream>>>(
-                xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty);
+                xp, wp, yp, ip, C, H, W, kH, kW, kcs, border, tx, ty, marks);
         }
+        SB_CUDA(cudaGetLastError());
+        return marks != nullptr;
     } else {
         if constexpr (!std::is_same<T, double>::value) {
             if (kH == kW && g.N * g.C < (1ll << 31) / 4096 && g.H * g.W < (1ll << 31)) {

@@ -127,6 +127,46 @@ __global__ void __launch_bounds__(256) element_fwd_kernel(const T* __restrict__ 
 // load serve four taps.  An SE row is walked only over its span of finite weights: a -inf weight never
 // wins (x + -inf for dilation, x - -inf for erosion), which skips most of a mask SE's corners.
 // ------------------------------------------------------------------------------------------------
+// Target-map marking inside a tiled forward (`map` non-null, with records): the winners of a tile's
+// outputs lie in its halo, so a CTA sets them in a shared bitmap of the halo's rows, in whole target-map
+// words, and ORs the non-zero words into the map at the end (a winner folded from beyond the halo goes
+// straight to the map).
+__host__ __device__ inline int mark_words(int tile_cols, int kW) { return (tile_cols + kW - 2) / 32 + 2; }
+__host__ __device__ inline size_t mark_bytes(int tile_rows, int tile_cols, int kH, int kW) {
+    return static_cast<size_t>(tile_rows + kH - 1) * mark_words(tile_cols, kW) * sizeof(uint32_t);
+}
+__device__ __forceinline__ int floor_div32(int v) { return v >= 0 ? v / 32 : -((31 - v) / 32); }
+
+struct TileMarks {
+    uint32_t* bits;
+    int rbase, wbase, rows, words;
+    __device__ void clear(int tid, int nthr) const {
+        for (int i = tid; i < rows * words; i += nthr) bits[i] = 0u;
+    }
+    // winner of output (oh, ow) through direct tap t (>= 0)
+    __device__ void mark(uint32_t* map, long long plane, int H, int W, int kW, int aH, int aW, int border, int oh,
+                         int ow, int t) const {
+        const int di = t / kW;
+        int x = oh + di - aH, y = ow + (t - di * kW) - aW;
+        if (!resolve(x, H, border) || !resolve(y, W, border)) return;
+        const int ri = x - rbase, wi = (y >> 5) - wbase;
+        if (ri >= 0 && ri < rows && wi >= 0 && wi < words)
+            atomicOr(&bits[ri * words + wi], 1u << (y & 31));
+        else
+            atomicOr(&map[(plane * H + x) * ((W + 31) / 32) + (y >> 5)], 1u << (y & 31));
+    }
+    __device__ void flush(uint32_t* map, long long plane, int H, int W, int tid, int nthr) const {
+        const int WW = (W + 31) / 32;
+        for (int i = tid; i < rows * words; i += nthr) {
+            const uint32_t v = bits[i];
+            if (v) {
+                const int ri = i / words;
+                atomicOr(&map[(plane * H + rbase + ri) * WW + wbase + (i - ri * words)], v);
+            }
+        }
+    }
+};
+
 constexpr int kTileQuad = 4;  // adjacent outputs per thread
 
 // staged row pitch: odd, so that the 4 rows x 8 column groups of a warp hit distinct banks
@@ -140,7 +180,7 @@ template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX>
 __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                         T* __restrict__ y, I* __restrict__ win, int C, int H, int W,
                                                         int kH, int kW, int kcs, int border, int tiles_x,
-                                                        int tiles_y) {
+                                                        int tiles_y, uint32_t* __restrict__ map) {
     using A = typename Storage<T>::acc;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int sw = tiled_pitch(kW), sh = kTile + kH - 1;
@@ -159,6 +199,9 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
     const A neutral = Op<OP>::template neutral<A>();
     const A never = -std::numeric_limits<A>::infinity();  // a weight that never wins
 
+    const TileMarks marks{reinterpret_cast<uint32_t*>(smem_raw + (tiled_smem(kH, kW, sizeof(A)) + 15) / 16 * 16),
+                          oh0 - aH, floor_div32(ow0 - aW), kTile + kH - 1, mark_words(kTile, kW)};
+    if (map) marks.clear(tid, 256);
     if (tid == 0) exact_flag = 1;
     __syncthreads();
     for (int i = tid; i < kH * kW; i += 256) {
@@ -189,57 +232,64 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
 
     const int lr = tid >> 3, q0 = (tid & 7) * kTileQuad;  // output row, first of four columns
     const int oh = oh0 + lr;
-    if (oh >= H || ow0 + q0 >= W) return;
-    const bool exact = !NeedsExactCheck<T>::value || exact_flag;
-    A best[kTileQuad];
-    int tap[kTileQuad];
-    bool tie[kTileQuad];
+    const bool active = !(oh >= H || ow0 + q0 >= W);
+    if (active) {
+        const bool exact = !NeedsExactCheck<T>::value || exact_flag;
+        A best[kTileQuad];
+        int tap[kTileQuad];
+        bool tie[kTileQuad];
 #pragma unroll
-    for (int k = 0; k < kTileQuad; ++k) {
-        best[k] = neutral;
-        tap[k] = -1;
-        tie[k] = false;
-    }
-    for (int di = 0; di < kH; ++di) {
-        const int lo = span[2 * di], hi = span[2 * di + 1];
-        if (hi < lo) continue;
-        const A* row = xs + (lr + di) * sw + q0 + lo;
-        const A* wrow = ws + di * kW;
-        A s0 = row[0], s1 = row[1], s2 = row[2];
-        for (int dj = lo; dj <= hi; ++dj) {
-            const A s3 = row[dj - lo + 3];
-            const A wv = wrow[dj];
-            const A v[kTileQuad] = {Op<OP>::tap(s0, wv), Op<OP>::tap(s1, wv), Op<OP>::tap(s2, wv), Op<OP>::tap(s3, wv)};
+        for (int k = 0; k < kTileQuad; ++k) {
+            best[k] = neutral;
+            tap[k] = -1;
+            tie[k] = false;
+        }
+        for (int di = 0; di < kH; ++di) {
+            const int lo = span[2 * di], hi = span[2 * di + 1];
+            if (hi < lo) continue;
+            const A* row = xs + (lr + di) * sw + q0 + lo;
+            const A* wrow = ws + di * kW;
+            A s0 = row[0], s1 = row[1], s2 = row[2];
+            for (int dj = lo; dj <= hi; ++dj) {
+                const A s3 = row[dj - lo + 3];
+                const A wv = wrow[dj];
+                const A v[kTileQuad] = {Op<OP>::tap(s0, wv), Op<OP>::tap(s1, wv), Op<OP>::tap(s2, wv), Op<OP>::tap(s3, wv)};
 #pragma unroll
-            for (int k = 0; k < kTileQuad; ++k) {
-                if (!exact) tie[k] |= v[k] == best[k];
-                if (Op<OP>::better(v[k], best[k])) {
-                    best[k] = v[k];
-                    tap[k] = di * kW + dj;
+                for (int k = 0; k < kTileQuad; ++k) {
+                    if (!exact) tie[k] |= v[k] == best[k];
+                    if (Op<OP>::better(v[k], best[k])) {
+                        best[k] = v[k];
+                        tap[k] = di * kW + dj;
+                    }
                 }
+                s0 = s1;
+                s1 = s2;
+                s2 = s3;
             }
-            s0 = s1;
-            s1 = s2;
-            s2 = s3;
+        }
+#pragma unroll
+        for (int k = 0; k < kTileQuad; ++k) {
+            const int ow = ow0 + q0 + k;
+            if (ow >= W) break;
+            if (!exact && tie[k] && best[k] != neutral) {
+                // a float tie with the running best: settle it the way the reference CPU does, in double
+                auto sample = [&](int di, int dj, A& s_) {
+                    s_ = xs[(lr + di) * sw + q0 + k + dj];
+                    return true;
+                };
+                auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
+                A b_;
+                window_winner<T, OP, true>(sample, weight, kH, kW, b_, tap[k]);
+            }
+            const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
+            if (WITH_VALUE) y[o] = Storage<T>::store(best[k]);
+            if (WITH_INDEX) win[o] = encode_direct<I>(tap[k]);
+            if (WITH_INDEX && map && tap[k] >= 0) marks.mark(map, tc.plane, H, W, kW, aH, aW, border, oh, ow, tap[k]);
         }
     }
-#pragma unroll
-    for (int k = 0; k < kTileQuad; ++k) {
-        const int ow = ow0 + q0 + k;
-        if (ow >= W) break;
-        if (!exact && tie[k] && best[k] != neutral) {
-            // a float tie with the running best: settle it the way the reference CPU does, in double
-            auto sample = [&](int di, int dj, A& s_) {
-                s_ = xs[(lr + di) * sw + q0 + k + dj];
-                return true;
-            };
-            auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
-            A b_;
-            window_winner<T, OP, true>(sample, weight, kH, kW, b_, tap[k]);
-        }
-        const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
-        if (WITH_VALUE) y[o] = Storage<T>::store(best[k]);
-        if (WITH_INDEX) win[o] = encode_direct<I>(tap[k]);
+    if (map) {
+        __syncthreads();
+        marks.flush(map, tc.plane, H, W, tid, 256);
     }
 }
 
@@ -266,7 +316,7 @@ template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX>
 __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                        T* __restrict__ y, I* __restrict__ win, int C, int H, int W,
                                                        int kH, int kW, int kcs, int border, int tiles_x,
-                                                       int tiles_y) {
+                                                       int tiles_y, uint32_t* __restrict__ map) {
     using A = typename Storage<T>::acc;
     constexpr int Q = kWideQ;
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -286,6 +336,9 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
     const A neutral = Op<OP>::template neutral<A>();
     const A never = -std::numeric_limits<A>::infinity();
 
+    const TileMarks marks{reinterpret_cast<uint32_t*>(smem_raw + (wide_smem(kH, kW, sizeof(A)) + 15) / 16 * 16),
+                          oh0 - aH, floor_div32(ow0 - aW), kWideRows + kH - 1, mark_words(kWideCols, kW)};
+    if (map) marks.clear(tid, 256);
     if (tid == 0) exact_flag = 1;
     __syncthreads();
     for (int i = tid; i < kH * kW; i += 256) {
@@ -321,113 +374,120 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
 
     const int lr = tid >> 3, c0 = (tid & 7) * Q;  // output row, first of eight columns
     const int oh = oh0 + lr;
-    if (oh >= H || ow0 + c0 >= W) return;
-    const bool exact = !NeedsExactCheck<T>::value || exact_flag;
-    A best[Q];
-    int tap[Q];
-    bool tie[Q];
+    const bool active = !(oh >= H || ow0 + c0 >= W);
+    if (active) {
+        const bool exact = !NeedsExactCheck<T>::value || exact_flag;
+        A best[Q];
+        int tap[Q];
+        bool tie[Q];
 #pragma unroll
-    for (int k = 0; k < Q; ++k) {
-        best[k] = neutral;
-        tap[k] = -1;
-        tie[k] = false;
-    }
-    for (int di = 0; di < kH; ++di) {
-        const int lo = info[3 * di], hi = info[3 * di + 1];
-        if (hi < lo) continue;
-        const A* row = xs + (lr + di) * sw + c0;  // output k's window starts at row[k]
-        const A* wrow = ws + di * kW;
-        if (info[3 * di + 2] && hi - lo + 1 >= Q) {
-            // suffix extrema of row[lo .. lo + Q - 2] (ties: the left one)
-            A sv[Q - 1];
-            int sc[Q - 1];
-            sv[Q - 2] = row[lo + Q - 2];
-            sc[Q - 2] = lo + Q - 2;
+        for (int k = 0; k < Q; ++k) {
+            best[k] = neutral;
+            tap[k] = -1;
+            tie[k] = false;
+        }
+        for (int di = 0; di < kH; ++di) {
+            const int lo = info[3 * di], hi = info[3 * di + 1];
+            if (hi < lo) continue;
+            const A* row = xs + (lr + di) * sw + c0;  // output k's window starts at row[k]
+            const A* wrow = ws + di * kW;
+            if (info[3 * di + 2] && hi - lo + 1 >= Q) {
+                // suffix extrema of row[lo .. lo + Q - 2] (ties: the left one)
+                A sv[Q - 1];
+                int sc[Q - 1];
+                sv[Q - 2] = row[lo + Q - 2];
+                sc[Q - 2] = lo + Q - 2;
 #pragma unroll
-            for (int k = Q - 3; k >= 0; --k) {
-                const A v = row[lo + k];
-                const bool take = !Op<OP>::better(sv[k + 1], v);
-                sv[k] = take ? v : sv[k + 1];
-                sc[k] = take ? lo + k : sc[k + 1];
-            }
-            // core row[lo + Q - 1 .. hi], first extremum
-            A cv = row[lo + Q - 1];
-            int cc = lo + Q - 1;
-            for (int j = lo + Q; j <= hi; ++j) {
-                const A v = row[j];
-                if (Op<OP>::better(v, cv)) {
-                    cv = v;
-                    cc = j;
+                for (int k = Q - 3; k >= 0; --k) {
+                    const A v = row[lo + k];
+                    const bool take = !Op<OP>::better(sv[k + 1], v);
+                    sv[k] = take ? v : sv[k + 1];
+                    sc[k] = take ? lo + k : sc[k + 1];
                 }
-            }
-            const A wz = wrow[lo];
-            A pv = neutral;
-            int pc = 0;
-#pragma unroll
-            for (int k = 0; k < Q; ++k) {
-                // window of output k: row[lo + k .. lo + Q - 2], the core, row[hi + 1 .. hi + k]
-                A rv = cv;
-                int rc = cc;
-                if (k < Q - 1 && !Op<OP>::better(cv, sv[k])) {
-                    rv = sv[k];
-                    rc = sc[k];
-                }
-                if (k > 0) {
-                    const A v = row[hi + k];
-                    if (k == 1 || Op<OP>::better(v, pv)) {
-                        pv = v;
-                        pc = hi + k;
-                    }
-                    if (Op<OP>::better(pv, rv)) {
-                        rv = pv;
-                        rc = pc;
+                // core row[lo + Q - 1 .. hi], first extremum
+                A cv = row[lo + Q - 1];
+                int cc = lo + Q - 1;
+                for (int j = lo + Q; j <= hi; ++j) {
+                    const A v = row[j];
+                    if (Op<OP>::better(v, cv)) {
+                        cv = v;
+                        cc = j;
                     }
                 }
-                const A t = Op<OP>::tap(rv, wz);
-                if (!exact) tie[k] |= t == best[k];
-                if (Op<OP>::better(t, best[k])) {
-                    best[k] = t;
-                    tap[k] = di * kW + rc - k;
-                }
-            }
-        } else {
-            A s[Q];
-#pragma unroll
-            for (int k = 0; k < Q - 1; ++k) s[k] = row[lo + k];
-            for (int dj = lo; dj <= hi; ++dj) {
-                s[Q - 1] = row[dj + Q - 1];
-                const A wv = wrow[dj];
+                const A wz = wrow[lo];
+                A pv = neutral;
+                int pc = 0;
 #pragma unroll
                 for (int k = 0; k < Q; ++k) {
-                    const A v = Op<OP>::tap(s[k], wv);
-                    if (!exact) tie[k] |= v == best[k];
-                    if (Op<OP>::better(v, best[k])) {
-                        best[k] = v;
-                        tap[k] = di * kW + dj;
+                    // window of output k: row[lo + k .. lo + Q - 2], the core, row[hi + 1 .. hi + k]
+                    A rv = cv;
+                    int rc = cc;
+                    if (k < Q - 1 && !Op<OP>::better(cv, sv[k])) {
+                        rv = sv[k];
+                        rc = sc[k];
+                    }
+                    if (k > 0) {
+                        const A v = row[hi + k];
+                        if (k == 1 || Op<OP>::better(v, pv)) {
+                            pv = v;
+                            pc = hi + k;
+                        }
+                        if (Op<OP>::better(pv, rv)) {
+                            rv = pv;
+                            rc = pc;
+                        }
+                    }
+                    const A t = Op<OP>::tap(rv, wz);
+                    if (!exact) tie[k] |= t == best[k];
+                    if (Op<OP>::better(t, best[k])) {
+                        best[k] = t;
+                        tap[k] = di * kW + rc - k;
                     }
                 }
+            } else {
+                A s[Q];
 #pragma unroll
-                for (int k = 0; k < Q - 1; ++k) s[k] = s[k + 1];
+                for (int k = 0; k < Q - 1; ++k) s[k] = row[lo + k];
+                for (int dj = lo; dj <= hi; ++dj) {
+                    s[Q - 1] = row[dj + Q - 1];
+                    const A wv = wrow[dj];
+#pragma unroll
+                    for (int k = 0; k < Q; ++k) {
+                        const A v = Op<OP>::tap(s[k], wv);
+                        if (!exact) tie[k] |= v == best[k];
+                        if (Op<OP>::better(v, best[k])) {
+                            best[k] = v;
+                            tap[k] = di * kW + dj;
+                        }
+                    }
+#pragma unroll
+                    for (int k = 0; k < Q - 1; ++k) s[k] = s[k + 1];
+                }
             }
         }
-    }
 #pragma unroll
-    for (int k = 0; k < Q; ++k) {
-        const int ow = ow0 + c0 + k;
-        if (ow >= W) break;
-        if (!exact && tie[k] && best[k] != neutral) {
-            // a float tie with the running best: settle it the way the reference CPU does, in double
-            auto sample = [&](int di, int dj, A& s_) {
-                s_ = xs[(lr + di) * sw + c0 + k + dj];
-                return true;
-            };
-            auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
-            A b_;
-            window_winner<T, OP, true>(sample, weight, kH, kW, b_, tap[k]);
+        for (int k = 0; k < Q; ++k) {
+            const int ow = ow0 + c0 + k;
+            if (ow >= W) break;
+            if (!exact && tie[k] && best[k] != neutral) {
+                // a float tie with the running best: settle it the way the reference CPU does, in double
+                auto sample = [&](int di, int dj, A& s_) {
+                    s_ = xs[(lr + di) * sw + c0 + k + dj];
+                    return true;
+                };
+                auto weight = [&](int di, int dj) { return ws[di * kW + dj]; };
+                A b_;
+                window_winner<T, OP, true>(sample, weight, kH, kW, b_, tap[k]);
+            }
+            const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
+            if (WITH_VALUE) y[o] = Storage<T>::store(best[k]);
+            if (WITH_INDEX) win[o] = encode_direct<I>(tap[k]);
+            if (WITH_INDEX && map && tap[k] >= 0) marks.mark(map, tc.plane, H, W, kW, aH, aW, border, oh, ow, tap[k]);
         }
-        const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
-        if (WITH_VALUE) y[o] = Storage<T>::store(best[k]);
-        if (WITH_INDEX) win[o] = encode_direct<I>(tap[k]);
+    }
+    if (map) {
+        __syncthreads();
+        marks.flush(map, tc.plane, H, W, tid, 256);
     }
 }
 
