@@ -143,12 +143,18 @@ struct TileMarks {
     __device__ void clear(int tid, int nthr) const {
         for (int i = tid; i < rows * words; i += nthr) bits[i] = 0u;
     }
-    // winner of output (oh, ow) through direct tap t (>= 0)
-    __device__ void mark(uint32_t* map, long long plane, int H, int W, int kW, int aH, int aW, int border, int oh,
-                         int ow, int t) const {
-        const int di = t / kW;
+    // winner of output (oh, ow) through direct tap t (>= 0); `last` holds the previous output's winner
+    // (plane-relative pixel, -1 for none), and an output with the same winner sets nothing
+    __device__ void mark(uint32_t* map, long long plane, int H, int W, int kW, uint32_t kw_magic, int aH, int aW,
+                         int border, int oh, int ow, int t, int& last) const {
+        const uint32_t ut = static_cast<uint32_t>(t);
+        const int di = kW == 1 ? t
+                               : static_cast<int>(ut <= 0xffffu ? __umulhi(ut, kw_magic) : ut / static_cast<uint32_t>(kW));
         int x = oh + di - aH, y = ow + (t - di * kW) - aW;
         if (!resolve(x, H, border) || !resolve(y, W, border)) return;
+        const int key = x * W + y;  // < H * W < 2^31
+        if (key == last) return;
+        last = key;
         const int ri = x - rbase, wi = (y >> 5) - wbase;
         if (ri >= 0 && ri < rows && wi >= 0 && wi < words)
             atomicOr(&bits[ri * words + wi], 1u << (y & 31));
@@ -267,6 +273,8 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
                 s2 = s3;
             }
         }
+        int last_winner = -1;  // marking: the previous output's winner pixel
+        const uint32_t kw_magic = kW > 1 ? static_cast<uint32_t>(((1ull << 32) + kW - 1) / kW) : 0u;
 #pragma unroll
         for (int k = 0; k < kTileQuad; ++k) {
             const int ow = ow0 + q0 + k;
@@ -284,7 +292,8 @@ __global__ void __launch_bounds__(256) tiled_fwd_kernel(const T* __restrict__ x,
             const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
             if (WITH_VALUE) y[o] = Storage<T>::store(best[k]);
             if (WITH_INDEX) win[o] = encode_direct<I>(tap[k]);
-            if (WITH_INDEX && map && tap[k] >= 0) marks.mark(map, tc.plane, H, W, kW, aH, aW, border, oh, ow, tap[k]);
+            if (WITH_INDEX && map && tap[k] >= 0)
+                marks.mark(map, tc.plane, H, W, kW, kw_magic, aH, aW, border, oh, ow, tap[k], last_winner);
         }
     }
     if (map) {
@@ -465,6 +474,8 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
                 }
             }
         }
+        int last_winner = -1;  // marking: the previous output's winner pixel
+        const uint32_t kw_magic = kW > 1 ? static_cast<uint32_t>(((1ull << 32) + kW - 1) / kW) : 0u;
 #pragma unroll
         for (int k = 0; k < Q; ++k) {
             const int ow = ow0 + c0 + k;
@@ -482,7 +493,8 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
             const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
             if (WITH_VALUE) y[o] = Storage<T>::store(best[k]);
             if (WITH_INDEX) win[o] = encode_direct<I>(tap[k]);
-            if (WITH_INDEX && map && tap[k] >= 0) marks.mark(map, tc.plane, H, W, kW, aH, aW, border, oh, ow, tap[k]);
+            if (WITH_INDEX && map && tap[k] >= 0)
+                marks.mark(map, tc.plane, H, W, kW, kw_magic, aH, aW, border, oh, ow, tap[k], last_winner);
         }
     }
     if (map) {
