@@ -827,7 +827,12 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                     uint8_t* din = worklist ? static_cast<uint8_t*>(tmp) : nullptr;
                     uint8_t* dout = worklist ? din + align256(blocks) : nullptr;
                     const size_t scan_smem = scan_tile_smem<typename Storage<T>::acc>();
-                    if (complete) set_smem(recon_tile_scan_kernel<T, OP>, scan_smem);
+                    if (complete) {
+                        // six tiles per SM: registers capped by the launch bounds, shared memory by the carveout
+                        set_smem(recon_tile_scan_kernel<T, OP>, scan_smem);
+                        SB_CUDA(cudaFuncSetAttribute(recon_tile_scan_kernel<T, OP>,
+                                                     cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+                    }
                     if (worklist && !converged) {
                         SB_CUDA(cudaMemsetAsync(din, 1, blocks, stream));
                         SB_CUDA(cudaMemsetAsync(dout, 0, blocks, stream));

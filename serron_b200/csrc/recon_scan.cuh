@@ -324,7 +324,7 @@ template <typename A>
 constexpr size_t scan_tile_smem() { return static_cast<size_t>((kScanTile + 2) + kScanTile) * (kScanTile + 3) * sizeof(A); }
 
 template <typename T, int OP>
-__global__ void __launch_bounds__(kScanTileThreads) recon_tile_scan_kernel(T* __restrict__ y, const T* __restrict__ mask, int H,
+__global__ void __launch_bounds__(kScanTileThreads, 6) recon_tile_scan_kernel(T* __restrict__ y, const T* __restrict__ mask, int H,
                                                               int W, int tiles_x, int tiles_y, int cls, int max_inner,
                                                               int* __restrict__ flags,
                                                               const uint8_t* __restrict__ dirty_in,
