@@ -12,16 +12,17 @@
 //                     selects (borders folded) and that pixel is marked.  Each finished band leaves
 //                     as one bit per pixel in the target map.  (The separable sweep forward sets the
 //                     map itself while it writes the records; then this launch is skipped.)
-//   pull_sum_kernel   computes grad_input.  A CTA owns a kSumTP x kPullTQ tile, reads its map words
-//                     (and writes zeros when they are empty), stages grad_output and the records
-//                     of the tile grown by the box halo in shared memory with cp.async, lists the set
+//   pull_sum_kernel   computes grad_input.  A CTA owns a kSumTP x kPullTQ tile, writes it as zeros
+//                     (16-byte stores), reads its map words (done when they are empty), stages
+//                     grad_output and the records of the tile grown by the box halo in shared memory
+//                     with cp.async, lists the set
 //                     bits, and one thread per winner p walks the (2aH+1) x (2aW+1) box of outputs around
 //                     p in raster order, adding grad_output of each output that selects p: exactly the
 //                     reference's sequence of additions for p, with no atomics and no ordering between
 //                     threads.  Inside the image an odd window's record IS the box tap of its winner,
 //                     (dr + aH) * kW + (dc + aW), so for boxes up to 15 x 15 the test runs on four
-//                     one-byte records at a time against constants, with the box unrolled.  The tile
-//                     leaves whole (zeros where nothing won), in 16-byte stores.
+//                     one-byte records at a time against constants, with the box unrolled.  Each
+//                     winner's sum is stored over the zeros.
 //
 // Every candidate must lie within a single border fold; the host sends windows wider than the image
 // under REFLECT elsewhere.
@@ -252,7 +253,7 @@ constexpr int kSumThreads = 128;
 // row, with a few bytes of slack behind the record row for word-wise reads.
 struct SumGeom {
     int aH, aW, hr, hq, gv, goff, gq, rv, roff, rq;
-    size_t go_b, rec_b, list_b, res_b;
+    size_t go_b, rec_b, list_b;
     __host__ __device__ SumGeom(int kH, int kW, int elem, int idx)
         : aH(kH / 2), aW(kW / 2), hr(kSumTP + 2 * (kH / 2)), hq(kPullTQ + 2 * (kW / 2)) {
         gv = 16 / elem;
@@ -264,9 +265,9 @@ struct SumGeom {
         go_b = (size_t(hr) * gq * elem + 15) / 16 * 16;
         rec_b = (size_t(hr) * rq * idx + 15) / 16 * 16;
         list_b = size_t(kSumTP) * kPullTQ * 2;
-        res_b = size_t(kSumTP) * kPullTQ * elem;
+
     }
-    __host__ __device__ size_t smem() const { return go_b + rec_b + list_b + res_b + 16; }
+    __host__ __device__ size_t smem() const { return go_b + rec_b + list_b + 16; }
 };
 
 // Sum for one pixel over its KB x KB box (KB = 2a + 1) of one-byte box taps staged in shared memory.
@@ -352,8 +353,7 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
     T* goS = reinterpret_cast<T*>(smem_raw);                                          // [hr][gq]
     I* recS = reinterpret_cast<I*>(smem_raw + geo.go_b);                              // [hr][rq]
     uint16_t* listS = reinterpret_cast<uint16_t*>(smem_raw + geo.go_b + geo.rec_b);   // [TP * TQ]
-    T* resS = reinterpret_cast<T*>(smem_raw + geo.go_b + geo.rec_b + geo.list_b);     // [TP][TQ]
-    int* countS = reinterpret_cast<int*>(smem_raw + geo.go_b + geo.rec_b + geo.list_b + geo.res_b);
+    int* countS = reinterpret_cast<int*>(smem_raw + geo.go_b + geo.rec_b + geo.list_b);
 
     const long long b = blockIdx.x;
     const int tx = static_cast<int>(b % tiles_x);
@@ -371,28 +371,24 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
         wcol = c0 / 32 + tid % (TQ / 32);
         if (wrow < H && wcol < WW) bits = map[(plane * H + wrow) * WW + wcol];
     }
-    // the tile leaves in 16-byte stores, from the result tile or (no winner in it) as zeros
+    // the tile is zeroed first, in 16-byte stores; the winners' sums are stored over the zeros after the
+    // barriers below (ordered within the CTA)
     T* gip = gi + plane * H * W;
-    auto write_tile = [&](bool zeros) {
+    {
         constexpr int OV = 16 / int(sizeof(T));
-        const uint4 zero4 = make_uint4(0, 0, 0, 0);
         for (int i = tid; i < TP * TQ / OV; i += NT) {
             const int pr = i / (TQ / OV), pc = (i - pr * (TQ / OV)) * OV;
             const int r = r0 + pr, c = c0 + pc;
             if (r >= H || c >= W) continue;
             T* dst = gip + static_cast<long long>(r) * W + c;
             if (out_vec && c + OV <= W) {
-                *reinterpret_cast<uint4*>(dst) = zeros ? zero4 : reinterpret_cast<const uint4*>(resS)[i];
+                *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
             } else {
-                for (int e = 0; e < OV && c + e < W; ++e) dst[e] = zeros ? Storage<T>::store(0.0f) : resS[pr * TQ + pc + e];
+                for (int e = 0; e < OV && c + e < W; ++e) dst[e] = Storage<T>::store(0.0f);
             }
         }
-    };
-    if (!__syncthreads_or(bits != 0u)) {  // no winner in the tile
-        write_tile(true);
-        return;
     }
-    for (int i = tid; i < int(geo.res_b / 16); i += NT) reinterpret_cast<uint4*>(resS)[i] = make_uint4(0, 0, 0, 0);
+    if (!__syncthreads_or(bits != 0u)) return;  // no winner in the tile
 
     // stage grad_output and records of output rows [r0 - aH, r0 + TP + aH) inside the image
     const T* gop = go + plane * H * W;
@@ -501,10 +497,8 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
                         acc = GradAcc<T>::add(acc, static_cast<G>(Storage<T>::load(grow[j])));
             }
         }
-        resS[p] = Storage<T>::store(static_cast<typename Storage<T>::acc>(acc));
+        gip[static_cast<long long>(x) * W + y] = Storage<T>::store(static_cast<typename Storage<T>::acc>(acc));
     }
-    __syncthreads();
-    write_tile(false);
 }
 
 // The box taps of a (kH, kW) window, and the "none" record, fit in a record of `idx` bytes.
