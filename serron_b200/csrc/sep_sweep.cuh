@@ -43,7 +43,10 @@ struct SweepGeom {
     static constexpr size_t XS_BYTES = ((size_t(TH) * XS * ELEM + 15) / 16) * 16;
     static constexpr size_t RD_END = ((2 * XS_BYTES + size_t(RR) * RS * 4 + size_t(RR) * RS) + 15) / 16 * 16;
     static constexpr int QCAP = 32 * K;  // winner-cell queue of a warp: one task's pushes at most
-    static constexpr size_t fwd_smem() { return RD_END + size_t(kSweepThreads / 32) * QCAP * 2; }
+    static constexpr size_t QUEUE_BYTES = size_t(kSweepThreads / 32) * QCAP * 2;
+    // the queues live in the step's staging buffer, dead once its row pass is done, where they fit
+    static constexpr bool QUEUE_IN_STAGE = XS_BYTES >= QUEUE_BYTES;
+    static constexpr size_t fwd_smem() { return RD_END + (QUEUE_IN_STAGE ? 0 : QUEUE_BYTES); }
 };
 
 // One run of K windows [m, m+K-1], m = 0..K-1, over samples v[0..2K-2]: value and first-extremum
@@ -104,7 +107,7 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
     T* const xsb1 = reinterpret_cast<T*>(smem_raw + G::XS_BYTES);
     float* rv = reinterpret_cast<float*>(smem_raw + 2 * G::XS_BYTES);   // [RR][RS]
     uint8_t* rdj = reinterpret_cast<uint8_t*>(rv + G::RR * RS);         // [RR][RS]
-    uint16_t* const queue = reinterpret_cast<uint16_t*>(smem_raw + G::RD_END) + (threadIdx.x >> 5) * G::QCAP;
+    uint16_t* const queue_own = reinterpret_cast<uint16_t*>(smem_raw + G::RD_END) + (threadIdx.x >> 5) * G::QCAP;
 
     const long long b = blockIdx.x;
     const int strip = static_cast<int>(b % strips);
@@ -173,7 +176,8 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
         }
     };
 
-    // the padding columns of both staging buffers never change: neutral once
+    // the padding columns of both staging buffers are never staged: neutral once (and again after a step
+    // whose winner queues lived in the buffer)
     for (int i = tid; i < 2 * TH * (XS - Cc); i += kSweepThreads) {
         const int r = i / (XS - Cc), q = Cc + i % (XS - Cc);
         (r < TH ? xsb0 : xsb1)[(r % TH) * XS + q] = neutral_t;
@@ -194,6 +198,9 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
     for (int s0 = oh_begin; s0 < oh_end; s0 += TH, ++step) {
         T* cur = (step & 1) ? xsb0 : xsb1;
         T* nxt = (step & 1) ? xsb1 : xsb0;
+        // (the next step's rows go to nxt, and cur is restaged only two steps on, after barriers)
+        uint16_t* const queue =
+            G::QUEUE_IN_STAGE ? reinterpret_cast<uint16_t*>(cur) + (threadIdx.x >> 5) * G::QCAP : queue_own;
         __syncthreads();  // nxt is no longer read
         if constexpr (ASYNC) {
             if (s0 + TH < oh_end) stage(nxt, s0 + TH - a + K - 1, TH);
@@ -264,6 +271,10 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
             }
         }
         __syncthreads();
+        // the queues overwrote cur: its padding columns back to neutral before its next row pass
+        if (G::QUEUE_IN_STAGE && marking)
+            for (int i = tid; i < TH * (XS - Cc); i += kSweepThreads)
+                cur[(i / (XS - Cc)) * XS + Cc + i % (XS - Cc)] = neutral_t;
         // carry the last K-1 row results to the top
         for (int i = tid; i < (K - 1) * RS; i += kSweepThreads) {
             rv[i] = rv[TH * RS + i];
