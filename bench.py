@@ -41,8 +41,8 @@ PRIMS = 2  # primitive calls per step
 # the backward's launch of the winners' sums
 FWD_BYTES_PER_PX = 4 + 4 + 1  # read x, write y, write winners
 BWD_BYTES_PER_PX = 4 + 1 + 4  # read grad_output, read winners, write grad_input
-# per-call DRAM traffic of each stage at the full workload: dram__bytes_read + dram__bytes_write of a
-# 1/8-size capture (profiles/gather_pull_and_sweep_fwd_batch4.md), times 8
+# per-call DRAM traffic of each stage at the full workload: dram__bytes_read + dram__bytes_write of an
+# ncu capture of the batch-4 workload (1/8 of the pixels), times 8
 NCU_TRAFFIC_BYTES = {"forward": 4.60e9, "gather": 4.64e9}
 LAUNCHES_PER_STEP = 2 * (1 + 1)  # per op: the forward, then the gather's sum kernel
 CPU_SAMPLE = (1, 64, 512, 512)  # one image of the batch: the slice the CPU baseline times (scaled by pixels)

@@ -202,8 +202,9 @@ SERRON_API int64_t serron_reconstruct_workspace_bytes(const int64_t* sizes, int6
  * Same arguments and results as serron_erode_backward / serron_dilate_backward (`op` selects which),
  * with the workspace taken from a fixed array of SERRON_STATIC_SCRATCH_BYTES per device that the
  * library reserves when it loads on that device.  A call needing more is rejected with
- * SERRON_ERR_WORKSPACE before anything is enqueued.  The first call on a device looks the array up
- * and may load the library's module there: make it before any stream capture.  All calls on a device
+ * SERRON_ERR_WORKSPACE before anything is enqueued.  Every call looks the array's address up with
+ * the device current (so a device reset between calls is harmless); the first call on a device may
+ * load the library's module there: make it before any stream capture.  All calls on a device
  * share the array, so calls that can overlap on the GPU (two streams, two host threads) race: order
  * them on one stream or with events.  Nothing in the array needs clearing between calls.
  * --------------------------------------------------------------------------------------------- */

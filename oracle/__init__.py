@@ -52,6 +52,8 @@ def _load() -> ctypes.CDLL:
         lib.oracle_backward.restype = ci
         lib.oracle_reconstruct.argtypes = [ci, ci, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, ci, ci, i64, i64]
         lib.oracle_reconstruct.restype = i64
+        lib.oracle_reconstruct_flood.argtypes = [ci, ci, vp, vp, vp, vp, i64, i64, i64, i64, i64, i64, i64, ci]
+        lib.oracle_reconstruct_flood.restype = ci
         _lib = lib
     return _lib
 
@@ -152,6 +154,44 @@ def reconstruct(dilate: bool, marker: torch.Tensor, mask: torch.Tensor, w: torch
     if steps < 0:
         raise RuntimeError(f"oracle: no fixed point after {max_iter} iterations")
     return out, int(steps)
+
+
+def reconstruct_flood(dilate: bool, marker: torch.Tensor, mask: torch.Tensor, w: torch.Tensor, border: int
+                      ) -> torch.Tensor:
+    """The fixed point ``reconstruct`` reaches, found by a max-heap flood (exact, O(n log n)).
+
+    Only for structuring elements whose finite taps weigh zero and include the anchor (cross, square,
+    diamond, disk masks) under the CONSTANT border, and inputs without NaN; it then equals the
+    reference's loop bit for bit and finishes images far too large for that loop on a CPU.
+    """
+    marker, mask, w = _prep(marker, mask, w)
+    out = torch.empty_like(marker)
+    rc = _load().oracle_reconstruct_flood(int(dilate), _DTYPE_CODE[marker.dtype], marker.data_ptr(), mask.data_ptr(),
+                                          w.data_ptr(), out.data_ptr(), *_geometry(marker, w), border)
+    if rc:
+        raise ValueError("oracle_reconstruct_flood: needs zero-weight finite taps with the anchor, CONSTANT, no NaN")
+    return out
+
+
+def blob_mask(n: int, *, blobs: int = 64, seeds: int = 32, seed: int = 0) -> tuple[torch.Tensor, torch.Tensor]:
+    """(marker, mask) of the large-image reconstruction workload, built on the CPU.
+
+    mask: ``blobs`` separable Gaussians (centres uniform over the image, sigma 20 + 180 * U, amplitude U)
+    summed in float64, rounded to float32, plus 0.05 * U noise; marker: zeros with ``seeds`` pixels copied
+    from the mask.  All draws from ``torch.Generator().manual_seed(seed)`` in that order.
+    """
+    cg = torch.Generator().manual_seed(seed)
+    cy, cx = torch.rand(blobs, generator=cg) * n, torch.rand(blobs, generator=cg) * n
+    sigma, amp = 20 + 180 * torch.rand(blobs, generator=cg), torch.rand(blobs, generator=cg)
+    ax = torch.arange(n, dtype=torch.float64)
+    gy = torch.exp(-((ax[None, :] - cy[:, None].double()) ** 2) / (2 * sigma[:, None].double() ** 2))
+    gx = torch.exp(-((ax[None, :] - cx[:, None].double()) ** 2) / (2 * sigma[:, None].double() ** 2))
+    mask = torch.einsum("k,ky,kx->yx", amp.double(), gy, gx).float().view(1, 1, n, n)
+    mask += 0.05 * torch.rand(1, 1, n, n, generator=cg)
+    marker = torch.zeros_like(mask)
+    idx = torch.randperm(n * n, generator=cg)[:seeds]
+    marker.view(-1)[idx] = mask.view(-1)[idx]
+    return marker, mask
 
 
 def reference_ops():

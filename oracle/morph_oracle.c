@@ -592,3 +592,162 @@ int64_t oracle_reconstruct(int dilate, int dtype, const void* marker, const void
     }
     return result;
 }
+
+/* ------------------------------------------------------------------------- */
+/* reconstruction to the fixed point by flooding (exact, any schedule)        */
+/* ------------------------------------------------------------------------- */
+
+/* The reference iterates y <- clip(op(y), mask) from clip(marker, mask) until
+ * nothing changes (torch-ext/serron/functional.py:144-202).  For a structuring
+ * element whose finite taps all weigh zero and include the anchor, under the
+ * CONSTANT border (out-of-image taps are neutral), a step only moves values
+ * along the taps' edges, so the fixed point is unique: for dilation, y(p) is the
+ * largest over paths q -> ... -> p (each node reading the previous through a
+ * tap) of min(y0(q), mask of every later node).  That is a widest-path problem,
+ * solved here by a max-heap flood in O(n log n) instead of thousands of full
+ * steps; erosion is the same on negated values.  Only min/max and copies are
+ * involved, so the result is bit-identical to the reference's loop.
+ * Returns 0, or -2 for arguments outside that class (another border, a
+ * non-zero finite weight, a missing anchor tap, NaN). */
+
+typedef struct {
+    double key;
+    uint32_t idx;
+} flood_item;
+
+static void flood_push(flood_item** heap, int64_t* n, int64_t* cap, double key, uint32_t idx) {
+    if (*n == *cap) {
+        *cap = *cap ? 2 * *cap : 1024;
+        *heap = realloc(*heap, (size_t)*cap * sizeof(flood_item));
+    }
+    flood_item* h = *heap;
+    int64_t i = (*n)++;
+    while (i > 0) {
+        const int64_t parent = (i - 1) / 2;
+        if (h[parent].key >= key) break;
+        h[i] = h[parent];
+        i = parent;
+    }
+    h[i].key = key;
+    h[i].idx = idx;
+}
+
+static flood_item flood_pop(flood_item* h, int64_t* n) {
+    const flood_item top = h[0];
+    const flood_item last = h[--(*n)];
+    int64_t i = 0;
+    for (;;) {
+        int64_t c = 2 * i + 1;
+        if (c >= *n) break;
+        if (c + 1 < *n && h[c + 1].key > h[c].key) ++c;
+        if (h[c].key <= last.key) break;
+        h[i] = h[c];
+        i = c;
+    }
+    if (*n > 0) h[i] = last;
+    return top;
+}
+
+int oracle_reconstruct_flood(int dilate, int dtype, const void* marker, const void* mask, const void* w, void* out,
+                             int64_t N, int64_t C, int64_t H, int64_t W, int64_t kH, int64_t kW, int64_t kcs,
+                             int border) {
+    if (check_args(0, dtype, border) || border != OR_CONSTANT) return -2;
+    const int64_t total = N * C * H * W, nk = kcs ? C * kcs : kH * kW, plane = H * W;
+    if (plane >= ((int64_t)1 << 32)) return -2;
+    const int64_t aH = kH / 2, aW = kW / 2;
+    double* wk = malloc(8 * (size_t)(nk > 0 ? nk : 1));
+    double* mk = malloc(8 * (size_t)(total > 0 ? total : 1));
+    double* y = malloc(8 * (size_t)(total > 0 ? total : 1));
+    float* tmpf = malloc(4 * (size_t)((total > nk ? total : nk) > 0 ? (total > nk ? total : nk) : 1));
+    int rc = 0;
+    /* widen to double (exact for every storage type) */
+    if (is_wide(dtype)) {
+        widen_d(dtype, w, wk, nk);
+        widen_d(dtype, mask, mk, total);
+        widen_d(dtype, marker, y, total);
+    } else {
+        widen_f(dtype, w, tmpf, nk);
+        for (int64_t i = 0; i < nk; ++i) wk[i] = tmpf[i];
+        widen_f(dtype, mask, tmpf, total);
+        for (int64_t i = 0; i < total; ++i) mk[i] = tmpf[i];
+        widen_f(dtype, marker, tmpf, total);
+        for (int64_t i = 0; i < total; ++i) y[i] = tmpf[i];
+    }
+    for (int64_t i = 0; i < nk; ++i)
+        if (!(wk[i] == 0.0 || (isinf(wk[i]) && wk[i] < 0))) rc = -2;
+    for (int64_t c = 0; c < (kcs ? C : 1) && !rc; ++c)
+        if (wk[c * kH * kW + aH * kW + aW] != 0.0) rc = -2;
+    for (int64_t i = 0; i < total && !rc; ++i)
+        if (isnan(mk[i]) || isnan(y[i])) rc = -2;
+    if (!rc) {
+        const double s = dilate ? 1.0 : -1.0; /* erosion: the same flood on negated values */
+        for (int64_t i = 0; i < total; ++i) {
+            mk[i] *= s;
+            y[i] *= s;
+            if (mk[i] < y[i]) y[i] = mk[i];
+        }
+        /* tap offsets of each plane's SE: u = v + (di - aH, dj - aW) is read by v */
+        int64_t* tdi = malloc(8 * (size_t)(kH * kW));
+        int64_t* tdj = malloc(8 * (size_t)(kH * kW));
+        flood_item* heap = NULL;
+        int64_t cap = 0;
+        for (int64_t pl = 0; pl < N * C; ++pl) {
+            const double* wp = wk + (kcs ? (pl % C) * kcs : 0);
+            int64_t nt = 0;
+            for (int64_t di = 0; di < kH; ++di)
+                for (int64_t dj = 0; dj < kW; ++dj)
+                    if (wp[di * kW + dj] == 0.0 && !(di == aH && dj == aW)) {
+                        tdi[nt] = di - aH;
+                        tdj[nt] = dj - aW;
+                        ++nt;
+                    }
+            double* yp = y + pl * plane;
+            const double* mp = mk + pl * plane;
+            int64_t n = 0;
+            /* every pixel that can raise a reader starts in the heap */
+            for (int64_t v = 0; v < plane; ++v) {
+                const int64_t vy = v / W, vx = v % W;
+                int raises = 0;
+                for (int64_t t = 0; t < nt && !raises; ++t) {
+                    const int64_t ry = vy - tdi[t], rx = vx - tdj[t];
+                    if (ry < 0 || ry >= H || rx < 0 || rx >= W) continue;
+                    const int64_t r = ry * W + rx;
+                    const double cand = yp[v] < mp[r] ? yp[v] : mp[r];
+                    raises = cand > yp[r];
+                }
+                if (raises) flood_push(&heap, &n, &cap, yp[v], (uint32_t)v);
+            }
+            while (n > 0) {
+                const flood_item it = flood_pop(heap, &n);
+                if (it.key != yp[it.idx]) continue; /* superseded by a later raise */
+                const int64_t uy = it.idx / W, ux = it.idx % W;
+                for (int64_t t = 0; t < nt; ++t) {
+                    /* the reader r of u through tap t: r + (di, dj) = u */
+                    const int64_t ry = uy - tdi[t], rx = ux - tdj[t];
+                    if (ry < 0 || ry >= H || rx < 0 || rx >= W) continue;
+                    const int64_t r = ry * W + rx;
+                    const double cand = it.key < mp[r] ? it.key : mp[r];
+                    if (cand > yp[r]) {
+                        yp[r] = cand;
+                        flood_push(&heap, &n, &cap, cand, (uint32_t)r);
+                    }
+                }
+            }
+        }
+        free(heap);
+        free(tdi);
+        free(tdj);
+        for (int64_t i = 0; i < total; ++i) y[i] *= s;
+        if (is_wide(dtype)) {
+            narrow_d(dtype, y, out, total);
+        } else {
+            for (int64_t i = 0; i < total; ++i) tmpf[i] = (float)y[i];
+            narrow_f(dtype, tmpf, out, total);
+        }
+    }
+    free(wk);
+    free(mk);
+    free(y);
+    free(tmpf);
+    return rc;
+}

@@ -2,13 +2,11 @@
 
 from __future__ import annotations
 
-from importlib.metadata import PackageNotFoundError
-from importlib.metadata import version as _version
 from typing import NotRequired, TypedDict
 
 import torch
 
-from . import _flatness
+from . import _flatness, _lib
 from ._ops import ops
 from .enums import Algorithm
 
@@ -61,19 +59,19 @@ def set_separable_min_k(like: torch.Tensor, min_k: int, *, backward: bool = Fals
 
 
 def device_fingerprint(device: torch.device | int | None = None) -> DeviceFingerprint:
-    """The GPU, toolkit and library version a tuning result belongs to."""
-    if not torch.cuda.is_available():
-        raise RuntimeError("serron: device_fingerprint needs a GPU")
+    """Where a measured algorithm choice is valid: this GPU model and SM count, its per-CTA shared
+    memory limit, the library build (package version and C-ABI version) and the CUDA toolkit."""
+    if isinstance(device, int):
+        device = torch.device("cuda", device)
+    if device is None or device.index is None:
+        if not torch.cuda.is_available():
+            raise RuntimeError("serron: a fingerprint describes a CUDA device, and none is visible")
+        device = torch.device("cuda", torch.cuda.current_device())
+    major, minor = torch.cuda.get_device_capability(device)
     props = torch.cuda.get_device_properties(device)
-    try:
-        lib_version = _version("serron_b200")
-    except PackageNotFoundError:
-        lib_version = "unknown"
-    return DeviceFingerprint(
-        name=props.name,
-        capability=f"{props.major}.{props.minor}",
-        sm_count=props.multi_processor_count,
-        max_optin_smem=int(getattr(props, "shared_memory_per_block_optin")),  # noqa: B009
-        serron=lib_version,
-        cuda=torch.version.cuda or "unknown",
-    )
+    from . import __version__
+
+    return DeviceFingerprint(name=torch.cuda.get_device_name(device), capability=f"{major}.{minor}",
+                             sm_count=props.multi_processor_count,
+                             max_optin_smem=props.shared_memory_per_block_optin,
+                             serron=f"{__version__}+abi{_lib.abi_version()}", cuda=str(torch.version.cuda))

@@ -1,8 +1,8 @@
 """Algorithm tuning (the public ``calibrate`` / ``autotune`` of packages/serron/torch-ext/serron/_autotune.py).
 
-The reference keeps a per-machine JSON cache and seeds per architecture; this build ships one
-measured default threshold for sm_100a inside the library and keeps tuning results for the process
-only.  :func:`calibrate` re-measures the separable crossover on the current GPU; :func:`autotune`
+The reference keeps a per-machine JSON cache and seeds per architecture; this build keeps tuning
+results for the process only, on top of the library's built-in window-length threshold for the
+separable path.  :func:`calibrate` re-measures the separable crossover on the current GPU; :func:`autotune`
 times every feasible algorithm on given problems and makes the autograd path force the winner.
 """
 

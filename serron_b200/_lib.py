@@ -125,6 +125,11 @@ def load() -> ctypes.CDLL:
         return lib
 
 
+def abi_version() -> int:
+    """Version of the C ABI the loaded library implements."""
+    return int(load().serron_abi_version())
+
+
 def sizes(shape) -> tuple[ctypes.Array, int]:
     """(int64 array, ndim) for a shape."""
     n = len(shape)

@@ -398,7 +398,9 @@ bool launch_forward_t(int algo, const Geometry& g, const void* x, const void* w,
         return marks != nullptr;
     } else {
         if constexpr (!std::is_same<T, double>::value) {
-            if (kH == kW && g.N * g.C < (1ll << 31) / 4096 && g.H * g.W < (1ll << 31)) {
+            // the sweep indexes a plane in 32 bits, including the masked rows a segment's last step runs
+            // past the image (fewer than 64)
+            if (kH == kW && g.N * g.C < (1ll << 31) / 4096 && (g.H + 64) * (g.W + 64) < (1ll << 31)) {
                 const int rc = sep_fast_fwd_t<T>(OP, kH, V, X, x, y, win, X ? map : nullptr, g.N * g.C, H, W, border,
                                                  stream);
                 if (rc > 0) SB_CUDA(static_cast<cudaError_t>(rc));

@@ -225,7 +225,8 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
             float v[2 * K - 1];
 #pragma unroll
             for (int m = 0; m < 2 * K - 1; ++m) v[m] = rv[(base + m) * RS + j];
-            // offsets within the plane fit in 32 bits (H * W < 2^31 is checked on the host)
+            // offsets within the plane fit in 32 bits, rows up to TH past the image included
+            // ((H + 64) * (W + 64) < 2^31 is checked on the host)
             const int o0 = (s0 + base) * W + ow;
             T* yp = y + plane * H * W;
             I* wp = win + plane * H * W;

@@ -11,8 +11,9 @@
 // Limits and rules of use
 //   - the scratch holds SERRON_STATIC_SCRATCH_BYTES (32 MiB) per device; a call whose workspace would
 //     be larger is rejected with SERRON_ERR_WORKSPACE before any work is enqueued;
-//   - the first call on each device looks the array's address up (cudaGetSymbolAddress with that
-//     device current), which may load the module: make that first call outside any stream capture;
+//   - every call looks the array's address up (cudaGetSymbolAddress with that device current), so an
+//     address never outlives the context it belongs to (a cudaDeviceReset between calls is fine); the
+//     first call on a device may load the module for it: make that first call outside any stream capture;
 //   - there is one array per device, so calls that can overlap on the GPU (on two streams, or from two
 //     host threads on one device) race on it: order such calls on one stream or with events;
 //   - nothing in the array has to start at zero: a call writes every scratch byte before reading it
@@ -21,7 +22,6 @@
 
 #include <cuda_runtime.h>
 
-#include <mutex>
 #include <sstream>
 #include <string>
 
@@ -34,26 +34,22 @@ namespace {
 constexpr int64_t kScratchBytes = SERRON_STATIC_SCRATCH_BYTES;
 __device__ __align__(256) unsigned char g_scratch[kScratchBytes];
 
-constexpr int kMaxDevices = 64;
-std::mutex g_mutex;
-void* g_scratch_address[kMaxDevices] = {};
-
-// Device address of g_scratch on `device`, looked up once per device with that device current.
+// Device address of g_scratch on `device`, looked up with that device current.  Only the failure of a
+// call made here is cleared from the runtime's last-error slot; an error the caller left pending stays.
 cudaError_t scratch_address(int device, void** out) {
-    const std::scoped_lock lock(g_mutex);
-    if (g_scratch_address[device] != nullptr) {
-        *out = g_scratch_address[device];
-        return cudaSuccess;
-    }
     int previous = -1;
-    if (cudaGetDevice(&previous) != cudaSuccess) previous = -1;
-    cudaGetLastError();
+    if (cudaGetDevice(&previous) != cudaSuccess) {
+        cudaGetLastError();
+        previous = -1;
+    }
     cudaError_t err = previous == device ? cudaSuccess : cudaSetDevice(device);
     void* address = nullptr;
     if (err == cudaSuccess) err = cudaGetSymbolAddress(&address, g_scratch);
     if (previous >= 0 && previous != device) cudaSetDevice(previous);
-    if (err != cudaSuccess) return err;
-    g_scratch_address[device] = address;
+    if (err != cudaSuccess) {
+        cudaGetLastError();
+        return err;
+    }
     *out = address;
     return cudaSuccess;
 }
@@ -72,8 +68,11 @@ extern "C" int serron_backward_static_scratch(int32_t op, const void* grad_outpu
         return SERRON_ERR_INVALID;
     }
     int count = 0;
-    if (cudaGetDeviceCount(&count) != cudaSuccess || device < 0 || device >= count || device >= kMaxDevices) {
+    if (cudaGetDeviceCount(&count) != cudaSuccess) {
         cudaGetLastError();
+        count = 0;
+    }
+    if (device < 0 || device >= count) {
         serron::set_last_error(std::string(name) + ": invalid device " + std::to_string(device));
         return SERRON_ERR_INVALID;
     }

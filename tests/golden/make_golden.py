@@ -37,7 +37,8 @@ import torch
 
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
-DEFAULT_REFERENCE = "/root/reference/packages/serron"
+# the reference's package sources: SERRON_REFERENCE_SOURCES, else a `reference` checkout beside this repository
+DEFAULT_REFERENCE = os.environ.get("SERRON_REFERENCE_SOURCES") or str(REPO.parent / "reference" / "packages" / "serron")
 
 BORDERS = {"reflect": 0, "replicate": 1, "constant": 2}
 DTYPES = {"float64": torch.float64, "float32": torch.float32, "float16": torch.float16, "bfloat16": torch.bfloat16}
