@@ -180,6 +180,75 @@ def run_reference(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_reference_cuda(args) -> None:
+    """The reference's own CUDA kernels (sm_100, compiled from its sources into oracle/_ref by
+    ``make -C oracle ref_cuda``) on this arm's workload and timing rules: each step is dilation and erosion,
+    each forward + backward, through the reference's operator API (its own bindings, loaded as
+    ``torch.ops.serron_ref``).  One small call is checked against the reference's CPU operators first."""
+    world, rank, local = _dist()
+    lib_dir = os.path.join(REPO, "oracle", "_ref")
+    cpu_lib, cuda_lib = os.path.join(lib_dir, "serron_ref_C.so"), os.path.join(lib_dir, "serron_ref_C_cuda.so")
+    if not (os.path.exists(cpu_lib) and os.path.exists(cuda_lib)):
+        if rank == 0:
+            print(json.dumps({"impl": "reference_cuda", "unavailable": "the reference's CUDA library was not built "
+                              "(make -C oracle ref_cuda)"}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = None
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    torch.ops.load_library(cpu_lib)
+    torch.ops.load_library(cuda_lib)
+    ref = torch.ops.serron_ref
+    w = torch.zeros(K, K, device=dev)
+    small = torch.rand(1, 2, 40, 48, generator=torch.Generator().manual_seed(1))
+    got = ref.dilate(small.to(dev), w, 0, True, 0).cpu()
+    if not torch.equal(got, ref.dilate(small, w.cpu(), 0, True, 0)):
+        raise SystemExit("bench.py: the reference's CUDA forward disagrees with its CPU forward")
+    gen = torch.Generator(device=dev).manual_seed(1000 + rank)
+    shape = (args.batch,) + SHAPE[1:]
+    x = torch.rand(*shape, device=dev, generator=gen)
+    go = torch.randn(*shape, device=dev, generator=gen)
+    px = shape[0] * shape[1] * shape[2] * shape[3]
+
+    def step() -> None:
+        for fwd, bwd in ((ref.dilate, ref.dilate_backward), (ref.erode, ref.erode_backward)):
+            fwd(x, w, 0, True, 0)
+            bwd(go, x, w, 0, True, False, 0)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        step()
+    b.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        print(json.dumps({"impl": "reference_cuda", "metric": METRIC, "value": px * PRIMS * world / (ms * 1e-3) / 1e9,
+                          "unit": "Gpix/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                          "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "dtype": "f32",
+                          "data": "synthetic", "config": {"workload": WORKLOAD, "per_gpu_batch": list(shape)},
+                          "note": "the reference's own sm_100 kernels (element/line passes, atomic scatter backward) "
+                                  "through its operator API"}), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_ours(args) -> None:
     world, rank, local = _dist()
     if not torch.cuda.is_available():
@@ -327,7 +396,10 @@ def run_ours(args) -> None:
         dominant = max(kernels, key=lambda n: kernels[n]["ms"])
         dk = kernels[dominant]
         line = {
-            "metric": METRIC, "value": value, "unit": "Gpix/s", "n_gpus": world, "steps": args.steps,
+            "metric": METRIC, "value": value, "value_per_gpu": value / world,
+            "value_note": "value is the whole job's output pixels per second over all GPUs; value_per_gpu divides it "
+                          "by n_gpus (the metric's per-GPU figure)",
+            "unit": "Gpix/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": WORKLOAD if shape == SHAPE else f"{WORKLOAD} (batch {shape[0]} instead of 32)",
@@ -383,12 +455,27 @@ def _config_inputs(cfg: int, dev: torch.device):
 
 
 def run_config(args) -> None:
-    """The other workloads, one GPU, device time per step (reported in the design notes, not by the driver)."""
+    """The other workloads, device time per step (reported in the design notes, not by the driver).
+
+    Under torchrun (N > 1): the learnable-layer workload (3) shards its batch of 64 along N and all-reduces
+    the structuring-element gradients (NCCL, rank-ordered sum) inside every timed step; the derived-ops
+    workload (4) shards its batch of 8; the reconstruction (5) shards the 8192 rows along H with a halo
+    exchange per round; the tiny workload (1) runs a replica per rank.  Time = max over ranks.
+    """
+    import datetime
+
     import serron_b200 as serron
 
-    dev = torch.device("cuda", 0)
+    world, rank, local = _dist()
+    dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
     from serron_b200 import _lib
+    from serron_b200.distributed import allreduce_se_grads, reconstruction_sharded, shard_bounds
 
     _lib.load()
     cfg = args.config
@@ -396,7 +483,7 @@ def run_config(args) -> None:
     B = serron.BorderMode
     if cfg == 1:
         x, k = d["x"], d["k"]
-        prims, px, bytes_px = 2, x.numel(), 8
+        prims, px, bytes_px = 2, x.numel() * world, 8
 
         def step():
             serron.dilation(serron.erosion(x, k, border=B.REPLICATE), k, border=B.REPLICATE)
@@ -404,19 +491,22 @@ def run_config(args) -> None:
         layer = serron.Opening2d(32, 7).to(dev)
         with torch.no_grad():
             layer.weight.copy_(d["w"])
-        x = d["x"].requires_grad_(True)
-        with torch.autocast("cuda"):
-            y0 = layer(x)
-        go = torch.randn(y0.shape, device=dev, generator=d["g"]).to(torch.float16)
-        prims, px, bytes_px = 2, x.numel(), 10
+        lo, hi = shard_bounds(d["x"].shape[0], rank, world)
+        x = d["x"][lo:hi].contiguous().requires_grad_(True)
+        go = torch.randn(d["x"].shape, device=dev, generator=d["g"]).to(torch.float16)[lo:hi].contiguous()
+        prims, px, bytes_px = 2, d["x"].numel(), 10
 
         def step():
+            layer.weight.grad = None
             with torch.autocast("cuda"):
                 y = layer(x)
-            torch.autograd.grad(y, (x, layer.weight), go)
+            y.backward(go)
+            if world > 1:
+                allreduce_se_grads(layer.parameters())
     elif cfg == 4:
-        x, k, gos = d["x"].requires_grad_(True), d["k"], d["go"]
-        prims, px, bytes_px = 6, x.numel(), 12
+        lo, hi = shard_bounds(d["x"].shape[0], rank, world)
+        x, k, gos = d["x"][lo:hi].contiguous().requires_grad_(True), d["k"], [g[lo:hi].contiguous() for g in d["go"]]
+        prims, px, bytes_px = 6, d["x"].numel(), 12
 
         def step():
             for fn, go in zip((serron.gradient, serron.top_hat, serron.black_hat), gos):
@@ -425,12 +515,21 @@ def run_config(args) -> None:
     else:
         marker, mask, k = d["marker"], d["mask"], d["k"]
         prims, px, bytes_px = 1, mask.numel(), 12
+        if world > 1:
+            lo, hi = shard_bounds(mask.shape[2], rank, world)
+            marker, mask = marker[:, :, lo:hi].contiguous(), mask[:, :, lo:hi].contiguous()
 
-        def step():
-            serron.reconstruction_by_dilation(marker, mask, k, border=B.CONSTANT)
+            def step():
+                reconstruction_sharded(marker, mask, k, border=B.CONSTANT)
+        else:
+            def step():
+                serron.reconstruction_by_dilation(marker, mask, k, border=B.CONSTANT)
 
     for _ in range(args.warmup):
         step()
+    torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
@@ -438,14 +537,25 @@ def run_config(args) -> None:
         step()
     b.record()
     torch.cuda.synchronize()
-    ms = a.elapsed_time(b) / args.steps
-    peak, peak_kind = _peaks()
-    line = {"config": cfg, "metric": "output Gpix/s" if cfg != 5 else "ms to the fixed point",
-            "value": px * prims / (ms * 1e-3) / 1e9 if cfg != 5 else ms, "ms_per_step": ms, "steps": args.steps,
-            "warmup": args.warmup, "pixels": px, "primitive_calls": prims,
-            "hbm_frac_of_algorithmic": (px * prims * bytes_px / (ms * 1e-3) / 1e9) / peak if cfg != 5 else None,
-            "peak_gbs": peak, "peak_source": peak_kind}
-    print(json.dumps(line), flush=True)
+    t = torch.tensor([a.elapsed_time(b) / args.steps], device=dev)
+    if dist:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    if rank == 0:
+        peak, peak_kind = _peaks()
+        line = {"config": cfg, "n_gpus": world, "metric": "output Gpix/s" if cfg != 5 else "ms to the fixed point",
+                "value": px * prims / (ms * 1e-3) / 1e9 if cfg != 5 else ms, "ms_per_step": ms,
+                "steps": args.steps, "warmup": args.warmup, "pixels": px, "primitive_calls": prims,
+                "scaling": "replicas" if cfg == 1 else "strong",
+                "collective": {3: "SE-grad all-gather + rank-ordered sum per step", 5: "halo send/recv + flag "
+                               "all-reduce per round"}.get(cfg) if world > 1 else None,
+                "hbm_frac_of_algorithmic": (px * prims * bytes_px / (ms * 1e-3) / 1e9) / (peak * world)
+                if cfg != 5 else None,
+                "peak_gbs": peak, "peak_source": peak_kind}
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
 
 
 def run_minmax_rate() -> None:
@@ -469,7 +579,7 @@ def main() -> None:
     p.add_argument("--gpus", type=int, default=1)
     p.add_argument("--steps", type=int, default=10)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--impl", choices=["ours", "reference", "reference_cuda"], default="ours")
     # a smaller leading dimension, for profiling captures that must stay within a few GB of device memory
     p.add_argument("--batch", type=int, default=SHAPE[0])
     # the other workloads (1, 3, 4, 5) for the design notes; the default run is workload 2
@@ -482,6 +592,8 @@ def main() -> None:
         run_config(args)
     elif args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference_cuda":
+        run_reference_cuda(args)
     else:
         run_ours(args)
 

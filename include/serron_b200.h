@@ -47,6 +47,7 @@ extern "C" {
 #define SERRON_ERR_CUDA 2          /* a CUDA runtime call failed */
 #define SERRON_ERR_NOT_CONVERGED 3 /* reconstruction: max_iter ran out */
 #define SERRON_ERR_WORKSPACE 4     /* workspace too small */
+#define SERRON_ERR_TIMEOUT 5       /* reconstruction: a bounded wait of the device worklist ran out */
 
 /* dtype codes */
 #define SERRON_F32 0
@@ -124,6 +125,20 @@ SERRON_API int serron_forward(int32_t op, const void* input, const int64_t* inpu
 /* Bytes of a record buffer of `winners_format` for an input of `sizes` (4-D): one record per output,
  * plus the target map when the format carries SERRON_WINNERS_MAP; -1 for bad arguments.  No
  * reference counterpart (the reference keeps no winner records). */
+/* The forward under CUDA autocast, with the backward's winners.  Replaces, for the calls it takes, the
+ * reference's autocast path: serron::erode/dilate on float16 casts of their arguments
+ * (packages/serron/torch-ext/serron/_cmake_ops.py:175-189) followed, in the backward, by a winner search
+ * on the saved tensors promoted to float32 (packages/serron/torch-ext/serron/autograd.py:37-76).
+ * `output` (float16, the shape of `input`) gets the op on the float16 casts of `input` (float32, float16
+ * or bfloat16, `input_dtype`) and `kernel` (float32); `winners` (serron_winners_bytes of `winners_format`,
+ * which must be the one serron_plan gives for the tiled algorithm: one-byte direct taps with the target
+ * map) gets the float32 winners, so serron_backward_from_winners can follow with a float32 grad_output.
+ * Windows: odd and square, 3 to 15.  The reference has no counterpart. */
+SERRON_API int serron_forward_autocast(int32_t op, const void* input, const int64_t* input_sizes, int64_t input_dim,
+                                       int32_t input_dtype, const void* kernel, const int64_t* kernel_sizes,
+                                       int64_t kernel_dim, int32_t kernel_dtype, int64_t border, void* output,
+                                       void* winners, int32_t winners_format, int32_t device, void* stream);
+
 SERRON_API int64_t serron_winners_bytes(const int64_t* sizes, int64_t dim, int32_t winners_format);
 
 /* ---------------------------------------------------------------------------------------------
@@ -176,13 +191,16 @@ SERRON_API int64_t serron_get_separable_min_k(int32_t device, int32_t dtype, int
  * Geodesic reconstruction.  Replaces the Python loop of serron.functional._reconstruct
  * (packages/serron/torch-ext/serron/functional.py:144-202): out = the fixed point of
  * clip(step(y), mask) from y = clip(marker, mask), step = dilate/clip = min when dilate != 0, else
- * erode/max.  With max_iter <= 0 the fixed point is found by row and column scans (flat SEs) and
- * tile-local relaxation over the tiles whose halo moved; with max_iter > 0
- * the reference's Jacobi schedule and check_every test are reproduced, so the call fails exactly when
- * the reference would.  Synchronous (reads a convergence flag).  *steps receives the number of
- * scan rounds and relaxation launches, or Jacobi steps, taken.  Workspace:
- * serron_reconstruct_workspace_bytes (256 bytes of flags, then two bytes per 64x64 tile for max_iter <= 0
- * or a second image for max_iter > 0).
+ * erode/max.  With max_iter <= 0 the fixed point is found by tile-local relaxation in one persistent
+ * launch over a device worklist of the 64x64 tiles whose halo moved (scan tiles for flat SEs within the
+ * 3x3 neighbourhood, after a few global row and column scan rounds for other flat SEs); the device
+ * decides convergence (no tile queued or running) and the host reads it once.  Every wait of that
+ * worklist is bounded (SERRON_RECON_WAIT_NS, default 2 s); one that runs out returns
+ * SERRON_ERR_TIMEOUT.  With max_iter > 0 the reference's Jacobi schedule and check_every test are
+ * reproduced, so the call fails exactly when the reference would.  Synchronous.  *steps receives the
+ * scan rounds plus tile runs, or the Jacobi steps, taken.  Workspace:
+ * serron_reconstruct_workspace_bytes (256 bytes of flags and counters, then for max_iter <= 0 a state
+ * word per tile and the worklist ring, for max_iter > 0 a second image).
  * --------------------------------------------------------------------------------------------- */
 SERRON_API int serron_reconstruct(int32_t dilate, const void* marker, const void* mask, const int64_t* sizes,
                                   int64_t dim, const void* kernel, const int64_t* kernel_sizes, int64_t kernel_dim,

@@ -20,6 +20,7 @@ ERR_INVALID = 1
 ERR_CUDA = 2
 ERR_NOT_CONVERGED = 3
 ERR_WORKSPACE = 4
+ERR_TIMEOUT = 5
 
 ERODE, DILATE = 0, 1
 
@@ -51,6 +52,7 @@ EXPORTED = (
     "serron_reconstruct_workspace_bytes",
     "serron_backward_static_scratch",
     "serron_winners_bytes",
+    "serron_forward_autocast",
 )
 
 
@@ -119,6 +121,8 @@ def load() -> ctypes.CDLL:
         lib.serron_reconstruct_workspace_bytes.restype = i64
         lib.serron_backward_static_scratch.argtypes = [i32] + bwd[:14] + [vp, vp, i32, vp]
         lib.serron_backward_static_scratch.restype = ctypes.c_int
+        lib.serron_forward_autocast.argtypes = [i32, vp, p64, i64, i32, vp, p64, i64, i32, i64, vp, vp, i32, i32, vp]
+        lib.serron_forward_autocast.restype = ctypes.c_int
         lib.serron_winners_bytes.argtypes = [p64, i64, i32]
         lib.serron_winners_bytes.restype = i64
         _lib = lib

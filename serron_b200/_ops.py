@@ -25,8 +25,8 @@ _NAMESPACE = "serron"
 # ------------------------------------------------------------------------------------------------
 # validation the C ABI cannot do (it sees pointers, not devices or dtypes)
 # ------------------------------------------------------------------------------------------------
-def _check_tensors(name: str, input_: torch.Tensor, kernel: torch.Tensor, grad_output: torch.Tensor | None = None
-                   ) -> None:
+def _check_tensors(name: str, input_: torch.Tensor, kernel: torch.Tensor, grad_output: torch.Tensor | None = None,
+                   *, same_dtype: bool = True) -> None:
     if grad_output is not None and not grad_output.is_cuda:
         raise RuntimeError(f"{name}: grad_output must be a CUDA tensor")
     if not input_.is_cuda:
@@ -39,7 +39,7 @@ def _check_tensors(name: str, input_: torch.Tensor, kernel: torch.Tensor, grad_o
         raise RuntimeError(f"{name}: grad_output must be 4-D (N, C, H, W), got {grad_output.dim()}-D")
     if kernel.dim() not in (2, 3):
         raise RuntimeError(f"{name}: kernel must be 2-D (kH, kW) or 3-D (C, kH, kW), got {kernel.dim()}-D")
-    if input_.dtype != kernel.dtype:
+    if same_dtype and input_.dtype != kernel.dtype:
         raise RuntimeError(f"{name}: input and kernel must share a dtype")
     if grad_output is not None and grad_output.dtype != input_.dtype:
         raise RuntimeError(f"{name}: grad_output and input must share a dtype")
@@ -111,6 +111,47 @@ def forward_with_winners(op: int, input_: torch.Tensor, kernel: torch.Tensor, bo
                                     winners.data_ptr(), p.winners_format, x.device.index, _lib.stream_of(x))
     _lib.raise_for(rc)
     return out, winners, p.winners_format
+
+
+# the direct one-byte record format with the gather's target map (what the tiled algorithm plans for
+# windows of up to 255 taps)
+_WINNERS_DIRECT_U8_MAP = 1 | 0x10
+
+
+def autocast_fused_ok(input_: torch.Tensor, kernel: torch.Tensor) -> bool:
+    """The autocast forward with float32 winners (:func:`forward_autocast`) takes this call."""
+    if input_.dim() != 4 or kernel.dim() not in (2, 3) or not (input_.is_cuda and kernel.is_cuda):
+        return False
+    if input_.dtype not in (torch.float32, torch.float16, torch.bfloat16) or kernel.dtype != torch.float32:
+        return False
+    kh, kw = kernel.shape[-2:]
+    if kh != kw or kh % 2 == 0 or not 3 <= kh <= 15:
+        return False
+    return kernel.dim() == 2 or kernel.shape[0] == input_.shape[1]
+
+
+def forward_autocast(op: int, input_: torch.Tensor, kernel: torch.Tensor, border: int
+                     ) -> tuple[torch.Tensor, torch.Tensor, int]:
+    """Forward on float16 casts of ``input_`` and ``kernel`` (CUDA autocast) with the records of the float32
+    winners, for a float32 :func:`backward_from_winners`."""
+    name = "serron::erode" if op == _lib.ERODE else "serron::dilate"
+    # the input and the float32 structuring element differ in dtype by design
+    _check_tensors(name, input_, kernel, same_dtype=False)
+    x = input_.contiguous()
+    k = kernel.contiguous()
+    out = torch.empty(x.shape, dtype=torch.float16, device=x.device)
+    xs, xd = _lib.sizes(x.shape)
+    lib = _lib.load()
+    nbytes = lib.serron_winners_bytes(xs, xd, _WINNERS_DIRECT_U8_MAP)
+    if nbytes < 0:
+        _lib.raise_for(_lib.ERR_INVALID)
+    winners = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    ks, kd = _lib.sizes(k.shape)
+    rc = lib.serron_forward_autocast(op, x.data_ptr(), xs, xd, _lib.DTYPE_CODE[x.dtype], k.data_ptr(), ks, kd,
+                                     _lib.DTYPE_CODE[k.dtype], int(border), out.data_ptr(), winners.data_ptr(),
+                                     _WINNERS_DIRECT_U8_MAP, x.device.index, _lib.stream_of(x))
+    _lib.raise_for(rc)
+    return out, winners, _WINNERS_DIRECT_U8_MAP
 
 
 def backward(op: int, grad_output: torch.Tensor, input_: torch.Tensor, kernel: torch.Tensor, border: int,

@@ -4,11 +4,13 @@ Contract as packages/serron/torch-ext/serron/autograd.py:32-123: the input and t
 element are promoted to their common dtype and saved; the backward casts ``grad_output`` to that dtype
 and returns grads only for the inputs that want them.
 
-B200 difference: when the forward runs in the saved dtype (no autocast cast in between), it also
-writes one winner record per output, and the backward gathers straight from those records instead of
-searching every window again.  Under CUDA autocast the forward computes in float16 while the backward
-works in the promoted dtype, exactly like the reference; the records would name float16 winners, so
-none are kept and the backward searches the windows itself.
+B200 difference: the forward also writes one winner record per output, and the backward gathers
+straight from those records instead of searching every window again.  Without autocast the records come
+from the forward itself.  Under CUDA autocast the value is computed on float16 casts while the backward
+works in the promoted dtype, exactly like the reference; for odd square windows of 3 to 15 with a
+float32 structuring element one kernel computes the float16 value and the promoted (float32) winners in
+the same pass (so the promoted copy of the input is never made); other autocast calls keep no records
+and the backward searches the windows itself.
 """
 
 from __future__ import annotations
@@ -39,20 +41,27 @@ def _autocast_cast(t: torch.Tensor) -> torch.Tensor:
 def _forward(ctx, op: int, input_: torch.Tensor, kernel: torch.Tensor, border: int, algo: int) -> torch.Tensor:
     ensure_loaded(input_.device)
     flat = _flatness.is_flat(kernel)
-    input_, kernel = _match_dtype(input_, kernel)
-    ctx.save_for_backward(input_, kernel)
     ctx.border = border
     ctx.flat = flat
     ctx.algo = int(algo)
     ctx.op = op
     ctx.winners = None
     ctx.winners_format = 0
+    # grad mode is off inside Function.forward; needs_input_grad says whether a backward can follow
+    wants_grad = any(ctx.needs_input_grad[:2])
+    ctx.dtype = torch.promote_types(input_.dtype, kernel.dtype)
+    if (wants_grad and int(algo) == 0 and input_.is_cuda and torch.is_autocast_enabled("cuda")
+            and ctx.dtype == torch.float32 and _ops.autocast_fused_ok(input_, kernel.to(ctx.dtype))):
+        kernel = kernel.to(ctx.dtype)
+        ctx.save_for_backward(kernel)
+        y, ctx.winners, ctx.winners_format = _ops.forward_autocast(op, input_, kernel, border)
+        return y
+    input_, kernel = _match_dtype(input_, kernel)
+    ctx.save_for_backward(kernel, input_)
     algo = int(algo) or select_algorithm(input_, kernel, flat, backward=False)
     x, k = input_, kernel
     if input_.is_cuda and torch.is_autocast_enabled("cuda"):
         x, k = _autocast_cast(input_), _autocast_cast(kernel)
-    # grad mode is off inside Function.forward; needs_input_grad says whether a backward can follow
-    wants_grad = any(ctx.needs_input_grad[:2])
     if wants_grad and x.dtype == input_.dtype and input_.is_cuda and kernel.is_cuda:
         y, ctx.winners, ctx.winners_format = _ops.forward_with_winners(op, x, k, border, flat, algo)
         return y
@@ -63,12 +72,13 @@ def _backward(ctx, grad_output: torch.Tensor):
     needs_input, needs_kernel = ctx.needs_input_grad[:2]
     if not (needs_input or needs_kernel):
         return None, None, None, None
-    input_, kernel = ctx.saved_tensors
-    grad_output = grad_output.to(input_.dtype).contiguous()
+    kernel = ctx.saved_tensors[0]
+    grad_output = grad_output.to(ctx.dtype).contiguous()
     if ctx.winners is not None:
         grad_input, grad_kernel = _ops.backward_from_winners(ctx.op, grad_output, ctx.winners, ctx.winners_format,
                                                              kernel, ctx.border, needs_kernel)
     else:
+        input_ = ctx.saved_tensors[1]
         algo = ctx.algo or select_algorithm(input_, kernel, ctx.flat, backward=True)
         grad_input, grad_kernel = _ops.backward(ctx.op, grad_output, input_, kernel, ctx.border, ctx.flat,
                                                 needs_kernel, algo)

@@ -11,6 +11,7 @@
 #include "common.cuh"
 #include "direct.cuh"
 #include "recon.cuh"
+#include "recon_persist.cuh"
 #include "recon_scan.cuh"
 #include "segrad.cuh"
 #include "separable.cuh"
@@ -24,6 +25,11 @@ namespace serron {
 template <typename T>
 int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win, uint32_t* map,
                    long long planes, int H, int W, int border, cudaStream_t stream);
+// the autocast forward (tiled_autocast.cu): float16 values and float32 winners in one pass
+bool autocast_fwd_supported_k(int kH, int kW);
+cudaError_t autocast_fwd_launch(int op, int input_dtype, int K, const void* x, const float* w, __half* y,
+                                uint8_t* win, uint32_t* map, long long planes, int C, int H, int W, int kcs,
+                                int border, int bulk, int out_vec, cudaStream_t stream);
 }  // namespace serron
 
 #include <algorithm>
@@ -556,12 +562,31 @@ void launch_gather_t(const Geometry& g, const void* go, const void* win, void* g
             const int go_vec = aligned(go) && (W * sizeof(T)) % 16 == 0;
             const int rec_vec = aligned(win) && (W * sizeof(I)) % 16 == 0;
             const int out_vec = aligned(gi) && (W * sizeof(T)) % 16 == 0;
-            auto sum = pull_sum_kernel<T, I>;
-            set_smem(sum, sgeo.smem());
-            SB_CUDA(cudaFuncSetAttribute(sum, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-            sum<<<grid_1d(g.N * g.C * tiles_x * tiles_y), kSumThreads, sgeo.smem(), stream>>>(
-                static_cast<const T*>(go), static_cast<const I*>(win), map, static_cast<T*>(gi), H, W, kH, kW, border,
-                tiles_x, tiles_y, go_vec, rec_vec, out_vec);
+            // rows of both staged arrays start on 16-byte boundaries: one bulk copy per row
+            const int bulk = go_vec && rec_vec;
+            auto run = [&](auto sum) {
+                set_smem(sum, sgeo.smem());
+                SB_CUDA(cudaFuncSetAttribute(sum, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+                sum<<<grid_1d(g.N * g.C * tiles_x * tiles_y), kSumThreads, sgeo.smem(), stream>>>(
+                    static_cast<const T*>(go), static_cast<const I*>(win), map, static_cast<T*>(gi), H, W, kH, kW,
+                    border, tiles_x, tiles_y, go_vec, rec_vec, out_vec, bulk);
+            };
+            // odd square windows up to 15 x 15 with one-byte records: the unrolled box of that size
+            const int box = (sizeof(I) == 1 && kH == kW && (kW & 1) && kW >= 3 && kW <= 15) ? kW : 0;
+            if constexpr (sizeof(I) == 1) {
+                switch (box) {
+                case 3: run(pull_sum_kernel<T, I, 3>); break;
+                case 5: run(pull_sum_kernel<T, I, 5>); break;
+                case 7: run(pull_sum_kernel<T, I, 7>); break;
+                case 9: run(pull_sum_kernel<T, I, 9>); break;
+                case 11: run(pull_sum_kernel<T, I, 11>); break;
+                case 13: run(pull_sum_kernel<T, I, 13>); break;
+                case 15: run(pull_sum_kernel<T, I, 15>); break;
+                default: run(pull_sum_kernel<T, I, 0>); break;
+                }
+            } else {
+                run(pull_sum_kernel<T, I, 0>);
+            }
             SB_CUDA(cudaGetLastError());
             return;
         }
@@ -722,6 +747,18 @@ int backward_impl(int op, const void* grad_output, const int64_t* go_sizes, int6
 // ------------------------------------------------------------------------------------------------
 // reconstruction
 // ------------------------------------------------------------------------------------------------
+// Wall-clock budget of each wait of the persistent worklist (a CTA waiting for a tile to be queued):
+// two seconds, or SERRON_RECON_WAIT_NS.  A healthy wait lasts at most a few tile runs per CTA of the
+// grid; one that runs out ends the call with SERRON_ERR_TIMEOUT instead of holding the GPU.
+unsigned long long recon_wait_budget_ns() {
+    if (const char* env = std::getenv("SERRON_RECON_WAIT_NS")) {
+        char* end = nullptr;
+        const unsigned long long v = std::strtoull(env, &end, 10);
+        if (end != env && *end == '\0' && v > 0) return v;
+    }
+    return 2000000000ull;
+}
+
 int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const int64_t* sizes, int64_t dim,
                      const void* kernel, const int64_t* k_sizes, int64_t k_dim, int32_t dtype, int64_t border,
                      int64_t max_iter, int64_t check_every, void* output, void* workspace, int64_t workspace_bytes,
@@ -773,10 +810,7 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                     const size_t smem = (static_cast<size_t>(kRecTile + kW - 1) * (kRecTile + kH - 1) +
                                          kRecTile * kRecTile + static_cast<size_t>(kH) * kW) *
                                         sizeof(typename Storage<T>::acc);
-                    auto kernel_fn = recon_tile_kernel<T, OP>;
-                    set_smem(kernel_fn, smem);
                     const long long blocks = static_cast<long long>(tx) * ty * g.N * g.C;
-                    const int64_t cap = 4 * (static_cast<int64_t>(H) * W + 16);
                     // a flat SE with an anchor and a direct neighbour: first rounds of row and column scans,
                     // which carry fronts across the image; when only the scans' taps exist and a round
                     // changes nothing, that is the fixed point
@@ -822,47 +856,57 @@ int reconstruct_impl(int32_t dilate, const void* marker, const void* mask, const
                             }
                         }
                     }
-                    // then tile relaxation to the fixed point, over a worklist of tiles whose halo moved
-                    // (when a halo reaches only the eight neighbours): tiles solved by scans in shared
-                    // memory when the scans cover the SE, else by the full step
-                    const bool worklist = complete || (kH < kRecTile && kW < kRecTile && H > kH && W > kW);
-                    uint8_t* din = worklist ? static_cast<uint8_t*>(tmp) : nullptr;
-                    uint8_t* dout = worklist ? din + align256(blocks) : nullptr;
-                    const size_t scan_smem = scan_tile_smem<typename Storage<T>::acc>();
-                    if (complete) {
-                        // six tiles per SM: registers capped by the launch bounds, shared memory by the carveout
-                        set_smem(recon_tile_scan_kernel<T, OP>, scan_smem);
-                        SB_CUDA(cudaFuncSetAttribute(recon_tile_scan_kernel<T, OP>,
-                                                     cudaFuncAttributePreferredSharedMemoryCarveout, 100));
-                    }
-                    if (worklist && !converged) {
-                        SB_CUDA(cudaMemsetAsync(din, 1, blocks, stream));
-                        SB_CUDA(cudaMemsetAsync(dout, 0, blocks, stream));
-                    }
-                    while (!converged) {
-                        SB_CUDA(cudaMemsetAsync(flags, 0, sizeof(int), stream));
-                        if (complete)
-                            recon_tile_scan_kernel<T, OP><<<grid_1d(blocks), kScanTileThreads, scan_smem, stream>>>(
-                                static_cast<T*>(output), static_cast<const T*>(mask), H, W, tx, ty, cls,
-                                4 * kRecTile, flags, din, dout);
-                        else
-                            kernel_fn<<<grid_1d(blocks), kRecThreads, smem, stream>>>(
-                                static_cast<T*>(output), static_cast<const T*>(mask), static_cast<const T*>(kernel),
-                                C, H, W, kH, kW, kcs, static_cast<int>(border), tx, ty, 4 * kRecTile, flags, din,
-                                dout);
+                    // then tile relaxation to the fixed point in one persistent launch: a device worklist of
+                    // tiles whose halo moved, solved by scans in shared memory when the scans cover the SE,
+                    // else by the full step; the fixed point is reached when no tile is queued or running
+                    if (!converged) {
+                        ReconQueue q;
+                        q.counters = reinterpret_cast<unsigned int*>(flags + 16);
+                        q.state = static_cast<int*>(tmp);
+                        q.cells = reinterpret_cast<unsigned long long*>(static_cast<char*>(tmp) + align256(4 * blocks));
+                        q.cap = static_cast<unsigned int>(recon_queue_cap(blocks));
+                        SB_CHECK(blocks < (1ll << 30), name, ": too many tiles for one call");
+                        recon_queue_init_kernel<<<grid_1d((q.cap + 255) / 256), 256, 0, stream>>>(q, static_cast<int>(blocks));
                         SB_CUDA(cudaGetLastError());
-                        ++taken;
-                        SB_CUDA(cudaMemcpyAsync(host_flags, flags, sizeof(int), cudaMemcpyDeviceToHost, stream));
+                        const unsigned long long budget = recon_wait_budget_ns();
+                        const int sms = device_info(device).sm_count;
+                        int per_sm = 0;
+                        if (complete) {
+                            using A = typename Storage<T>::acc;
+                            const size_t scan_smem = scan_tile_smem<A>();
+                            auto kfn = recon_persist_scan_kernel<T, OP>;
+                            // six tiles per SM: registers capped by the launch bounds, shared memory by the carveout
+                            set_smem(kfn, scan_smem);
+                            SB_CUDA(cudaFuncSetAttribute(kfn, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+                            SB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kScanTileThreads, scan_smem));
+                            const long long grid = std::min<long long>(blocks, std::min<long long>(kReconMaxGrid, std::max(1, per_sm) * sms));
+                            kfn<<<static_cast<unsigned>(grid), kScanTileThreads, scan_smem, stream>>>(
+                                static_cast<T*>(output), static_cast<const T*>(mask), H, W, tx, ty, cls, 4 * kRecTile, q,
+                                budget);
+                        } else {
+                            auto kfn = recon_persist_full_kernel<T, OP>;
+                            set_smem(kfn, smem);
+                            SB_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kfn, kRecThreads, smem));
+                            const long long grid = std::min<long long>(blocks, std::min<long long>(kReconMaxGrid, std::max(1, per_sm) * sms));
+                            // a halo within the eight neighbours, or (a window wider than a tile, or folded across an
+                            // image narrower than itself) the whole plane
+                            const int reach = (kH < kRecTile && kW < kRecTile && H > kH && W > kW) ? 1 : std::max(tx, ty);
+                            kfn<<<static_cast<unsigned>(grid), kRecThreads, smem, stream>>>(
+                                static_cast<T*>(output), static_cast<const T*>(mask), static_cast<const T*>(kernel), C, H,
+                                W, kH, kW, kcs, static_cast<int>(border), tx, ty, 4 * kRecTile, reach, q, budget);
+                        }
+                        SB_CUDA(cudaGetLastError());
+                        unsigned int counters[5] = {0, 0, 0, 0, 0};
+                        SB_CUDA(cudaMemcpyAsync(counters, q.counters, sizeof(counters), cudaMemcpyDeviceToHost, stream));
                         SB_CUDA(cudaStreamSynchronize(stream));
-                        if (host_flags[0] == 0) {
-                            converged = true;
-                            break;
-                        }
-                        SB_CHECK(taken < cap, name, ": relaxation did not settle");
-                        if (worklist) {
-                            std::swap(din, dout);
-                            SB_CUDA(cudaMemsetAsync(dout, 0, blocks, stream));
-                        }
+                        if (counters[3] != 0u)
+                            throw Failure{SERRON_ERR_TIMEOUT,
+                                          concat(name, ": a wait of the device worklist ran out after ", budget,
+                                                 " ns (status ", counters[3], "); the result is incomplete")};
+                        SB_CHECK(counters[2] == 0u, name, ": the device worklist ended with ", counters[2],
+                                 " tiles outstanding");
+                        taken += counters[4];
+                        converged = true;
                     }
                 } else {
                     // the reference's Jacobi schedule: check every `check_every` steps, stop at max_iter
@@ -939,6 +983,38 @@ int serron_forward(int32_t op, const void* input, const int64_t* input_sizes, in
                    int64_t algo, void* output, void* winners, int32_t winners_format, int32_t device, void* stream) {
     return forward_impl(op, input, input_sizes, input_dim, kernel, kernel_sizes, kernel_dim, dtype, border, flat, algo,
                         output, winners, winners_format, device, stream);
+}
+
+int serron_forward_autocast(int32_t op, const void* input, const int64_t* input_sizes, int64_t input_dim,
+                            int32_t input_dtype, const void* kernel, const int64_t* kernel_sizes, int64_t kernel_dim,
+                            int32_t kernel_dtype, int64_t border, void* output, void* winners, int32_t winners_format,
+                            int32_t device, void* stream) {
+    return guarded([&] {
+        SB_CHECK(op == kErode || op == kDilate, "serron: invalid op ", op);
+        const char* name = op_name(op);
+        const Geometry g = parse_geometry(name, input_sizes, input_dim, kernel_sizes, kernel_dim);
+        check_common(name, input_dtype, border);
+        SB_CHECK(input_dtype == kF32 || input_dtype == kF16 || input_dtype == kBF16, name,
+                 ": the autocast forward takes a float32, float16 or bfloat16 input");
+        SB_CHECK(kernel_dtype == kF32, name, ": the autocast forward needs a float32 structuring element");
+        SB_CHECK(autocast_fwd_supported_k(static_cast<int>(g.kH), static_cast<int>(g.kW)), name,
+                 ": the autocast forward needs an odd square window of 3 to 15, got ", g.kH, "x", g.kW);
+        const int fmt = winners_format_for(kTiled, g.kH, g.kW);
+        SB_CHECK(winners_format == fmt, name, ": winner format ", winners_format, " (", fmt, " expected)");
+        DeviceScope scope(device);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (g.numel() == 0) return;
+        SB_CHECK(input && kernel && output && winners, name, ": null tensor pointer");
+        uint32_t* map = reinterpret_cast<uint32_t*>(static_cast<char*>(winners) + records_bytes(g, fmt));
+        SB_CUDA(cudaMemsetAsync(map, 0, pull_map_words(g.N * g.C, g.H, g.W) * 4, s));
+        auto aligned = [](const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) & (n - 1)) == 0; };
+        const int bulk = aligned(input, 16) && (g.W * static_cast<int64_t>(elem_size(input_dtype))) % 16 == 0;
+        const int out_vec = aligned(output, 16) && aligned(winners, 8) && g.W % 8 == 0;
+        SB_CUDA(autocast_fwd_launch(op, input_dtype, static_cast<int>(g.kH), input, static_cast<const float*>(kernel),
+                                    static_cast<__half*>(output), static_cast<uint8_t*>(winners), map, g.N * g.C,
+                                    static_cast<int>(g.C), static_cast<int>(g.H), static_cast<int>(g.W),
+                                    static_cast<int>(g.kcs), static_cast<int>(border), bulk, out_vec, s));
+    });
 }
 
 int64_t serron_winners_bytes(const int64_t* sizes, int64_t dim, int32_t winners_format) {
@@ -1122,9 +1198,10 @@ int serron_reconstruct(int32_t dilate, const void* marker, const void* mask, con
 int64_t serron_reconstruct_workspace_bytes(const int64_t* sizes, int64_t dim, int32_t dtype, int64_t max_iter) {
     if (dim != 4 || sizes == nullptr || dtype < kF32 || dtype > kBF16) return -1;
     const int64_t total = sizes[0] * sizes[1] * sizes[2] * sizes[3];
-    // the Jacobi schedule's second buffer, or two dirty bytes per relaxation tile (read / set)
+    // the Jacobi schedule's second buffer, or the device worklist: a state word per tile and the ring
     const int64_t tiles = sizes[0] * sizes[1] * ((sizes[2] + kRecTile - 1) / kRecTile) * ((sizes[3] + kRecTile - 1) / kRecTile);
-    return 256 + (max_iter > 0 ? align256(total * static_cast<int64_t>(elem_size(dtype))) : 2 * align256(tiles));
+    return 256 + (max_iter > 0 ? align256(total * static_cast<int64_t>(elem_size(dtype)))
+                               : align256(4 * tiles) + align256(8 * recon_queue_cap(tiles)));
 }
 
 }  // extern "C"

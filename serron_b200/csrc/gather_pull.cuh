@@ -28,6 +28,7 @@
 // under REFLECT elsewhere.
 #pragma once
 
+#include "bulk_copy.cuh"
 #include "common.cuh"
 
 namespace serron {
@@ -336,12 +337,16 @@ __device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed_clip(const u
     return pull_box_fixed<KB, T>(rec, rq, gp, gq, rows_ok, keep);
 }
 
-template <typename T, typename I>
+// KB > 0: the box of a KB x KB window with one-byte records, unrolled (one kernel per size keeps each
+// one's code small); KB == 0: any window, walked generically.  With `bulk`, grad_output and the records
+// of each staged row arrive by one bulk copy each (rows 16-byte aligned: the host checks pointers and W).
+template <typename T, typename I, int KB>
 __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restrict__ go, const I* __restrict__ win,
                                                                const uint32_t* __restrict__ map,
                                                                T* __restrict__ gi, int H, int W, int kH, int kW,
                                                                int border, int tiles_x, int tiles_y, int go_vec,
-                                                               int rec_vec, int out_vec) {
+                                                               int rec_vec, int out_vec, int bulk) {
+    static_assert(KB == 0 || sizeof(I) == 1, "the unrolled box reads one-byte records");
     using G = typename GradAcc<T>::type;
     constexpr int TP = kSumTP, TQ = kPullTQ, NT = kSumThreads, NWORDS = TP * TQ / 32;
     constexpr uint32_t kNone = IndexTraits<I>::none;
@@ -394,7 +399,40 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
     const T* gop = go + plane * H * W;
     const I* wp = win + plane * H * W;
     const int lo = max(0, r0 - aH), hi = min(H, r0 + TP + aH);
-    {
+    __shared__ __align__(8) uint64_t bar;
+    if (bulk) {
+        // one bulk copy per row and array of the part inside the image; the columns outside it are filled
+        const int gcol0 = c0 - aW - goff, rcol0 = c0 - aW - roff;  // 16-byte aligned in the image row
+        const int gc_lo = max(gcol0, 0), gc_hi = min(gcol0 + gq, W);
+        const int rc_lo = max(rcol0, 0), rc_hi = min(rcol0 + rq, W);
+        const unsigned gbytes = static_cast<unsigned>(gc_hi - gc_lo) * sizeof(T);
+        const unsigned rbytes = static_cast<unsigned>(rc_hi - rc_lo) * sizeof(I);
+        if (tid == 0) {
+            mbar_init(&bar, 1);
+            mbar_arrive_expect_tx(&bar, (gbytes + rbytes) * static_cast<unsigned>(hi - lo));
+        }
+        __syncthreads();
+        for (int i = tid; i < 2 * (hi - lo); i += NT) {
+            const int h = lo + (i >> 1), sr = h - (r0 - aH);
+            if (i & 1)
+                bulk_load(recS + sr * rq + (rc_lo - rcol0), wp + static_cast<long long>(h) * W + rc_lo, rbytes, &bar);
+            else
+                bulk_load(goS + sr * gq + (gc_lo - gcol0), gop + static_cast<long long>(h) * W + gc_lo, gbytes, &bar);
+        }
+        if (gc_lo > gcol0 || gc_hi < gcol0 + gq || rc_lo > rcol0 || rc_hi < rcol0 + rq) {
+            const int gpad = gq - (gc_hi - gc_lo), rpad = rq - (rc_hi - rc_lo);
+            for (int i = tid; i < (hi - lo) * gpad; i += NT) {
+                const int sr = lo + i / gpad - (r0 - aH), q = i % gpad;
+                const int col = q < gc_lo - gcol0 ? q : gc_hi - gcol0 + (q - (gc_lo - gcol0));
+                goS[sr * gq + col] = Storage<T>::store(0.0f);
+            }
+            for (int i = tid; i < (hi - lo) * rpad; i += NT) {
+                const int sr = lo + i / rpad - (r0 - aH), q = i % rpad;
+                const int col = q < rc_lo - rcol0 ? q : rc_hi - rcol0 + (q - (rc_lo - rcol0));
+                recS[sr * rq + col] = static_cast<I>(kNone);
+            }
+        }
+    } else {
         const int nchg = gq / gv, nchr = rq / rv;
         const uint32_t mg = static_cast<uint32_t>(((1ull << 32) + nchg - 1) / nchg);  // i < 2^16: exact
         const uint32_t mr = static_cast<uint32_t>(((1ull << 32) + nchr - 1) / nchr);
@@ -441,50 +479,74 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
         const int pbase = (wrow - r0) * TQ + (wcol * 32 - c0);
         for (uint32_t m = bits; m; m &= m - 1) listS[pos++] = static_cast<uint16_t>(pbase + __ffs(m) - 1);
     }
-    pg_wait_all();
-    __syncthreads();
+    if (bulk) {
+        // a byte count that never arrives ends the wait: the tile is poisoned (NaN) instead of hanging
+        if (!__syncthreads_and(mbar_wait(&bar, 0))) {
+            for (int i = tid; i < TP * TQ; i += NT) {
+                const int r = r0 + i / TQ, c = c0 + i % TQ;
+                if (r < H && c < W) gip[static_cast<long long>(r) * W + c] = Storage<T>::store(__int_as_float(0x7fffffff));
+            }
+            return;
+        }
+    } else {
+        pg_wait_all();
+        __syncthreads();
+    }
 
     // records become box taps: (dr + aH) * S + (dc + aW) of the pixel each output selects.  An odd window's
     // record already is one unless a border folds its target, which only happens near the image edge.
     const bool folds = r0 - 2 * aH < 0 || r0 + TP + 2 * aH > H || c0 - 2 * aW < 0 || c0 + TQ + 2 * aW > W;
     if (folds || !(kW & 1)) {
         const uint32_t kw_magic = kW > 1 ? static_cast<uint32_t>(((1ull << 32) + kW - 1) / kW) : 0u;
-        const uint32_t mq = static_cast<uint32_t>(((1ull << 32) + hq - 1) / hq);
-        for (int i = tid; i < (hi - lo) * hq; i += NT) {
-            const int r = static_cast<int>(__umulhi(static_cast<uint32_t>(i), mq)), lw = i - r * hq;
-            const int h = lo + r, w = c0 - aW + lw;
-            if (static_cast<unsigned>(w) >= static_cast<unsigned>(W)) continue;
-            // an odd window inside the image selects a pixel inside it: its record is its box tap
-            if ((kW & 1) && h >= aH && h < H - aH && w >= aW && w < W - aW) continue;
+        auto convert = [&](int h, int lw) {
+            const int w = c0 - aW + lw;
+            if (static_cast<unsigned>(w) >= static_cast<unsigned>(W)) return;
             I& rec = recS[(h - (r0 - aH)) * rq + roff + lw];
             int x, y;
             if (!pg_target(rec, kNone, h, w, H, W, kW, aH, aW, border, kw_magic, x, y))
                 rec = static_cast<I>(kNone);
             else
                 rec = static_cast<I>((x - h + aH) * S + (y - w + aW));
+        };
+        if (!(kW & 1)) {
+            const uint32_t mq = static_cast<uint32_t>(((1ull << 32) + hq - 1) / hq);
+            for (int i = tid; i < (hi - lo) * hq; i += NT) {
+                const int r = static_cast<int>(__umulhi(static_cast<uint32_t>(i), mq));
+                convert(lo + r, i - r * hq);
+            }
+        } else {
+            // an odd window inside the image selects a pixel inside it, and its record already is its box
+            // tap: only the outputs within the window's half-width of an image edge are converted.  Rows
+            // [lo, e0) and [e1, hi) in full; the other rows' first and last columns.
+            const int e0 = min(hi, max(lo, aH)), e1 = max(e0, min(hi, H - aH));
+            const int edge_rows = (e0 - lo) + (hi - e1);
+            const int lw_l1 = max(0, min(hq, 2 * aW - c0));        // columns w < aW: lw < 2aW - c0
+            const int lw_r0 = max(lw_l1, min(hq, W - c0));         // columns w >= W - aW: lw >= W - c0
+            const int side = lw_l1 + (hq - lw_r0);
+            for (int i = tid; i < edge_rows * hq; i += NT) {
+                const int r = i / hq, lw = i - r * hq;
+                convert(r < e0 - lo ? lo + r : e1 + r - (e0 - lo), lw);
+            }
+            if (side > 0)
+                for (int i = tid; i < (e1 - e0) * side; i += NT) {
+                    const int r = i / side, k = i - r * side;
+                    convert(e0 + r, k < lw_l1 ? k : lw_r0 + (k - lw_l1));
+                }
         }
         __syncthreads();
     }
 
     // one thread per winner: the outputs of its box, in raster order
     const int n = *countS;
-    const bool box_fixed = sizeof(I) == 1 && kH == kW && (kW & 1) && kW >= 3 && kW <= 15;
     for (int k = tid; k < n; k += NT) {
         const int p = listS[k];
         const int pr = p / TQ, pc = p - pr * TQ;  // box rows pr .. pr + 2aH, columns pc .. pc + 2aW (staged)
         const int x = r0 + pr, y = c0 + pc;
         G acc = G(0);
-        if (box_fixed) {
+        if constexpr (KB > 0) {
             const uint8_t* rec = reinterpret_cast<const uint8_t*>(recS) + pr * rq + roff + pc;
             const T* gp = goS + pr * gq + goff + pc;
-            switch (kW) {
-#define SERRON_PULL_FIXED(KB) \
-    case KB: acc = pull_box_fixed_clip<KB, T>(rec, rq, gp, gq, x, y, H, W); break;
-                SERRON_PULL_FIXED(3) SERRON_PULL_FIXED(5) SERRON_PULL_FIXED(7) SERRON_PULL_FIXED(9)
-                SERRON_PULL_FIXED(11) SERRON_PULL_FIXED(13) SERRON_PULL_FIXED(15)
-#undef SERRON_PULL_FIXED
-            default: break;
-            }
+            acc = pull_box_fixed_clip<KB, T>(rec, rq, gp, gq, x, y, H, W);
         } else {
             for (int h = max(0, x - aH); h <= min(H - 1, x + aH); ++h) {
                 const int lh = h - (r0 - aH);

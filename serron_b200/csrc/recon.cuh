@@ -6,19 +6,33 @@
 //
 // The step map is monotone and the iteration starts below its least fixed point (the anchor tap is
 // >= 0), so every schedule that keeps applying the step to some pixels until none changes reaches the
-// same fixed point.  `recon_tile_kernel` exploits that: each CTA loads a tile plus halo, iterates it in
-// shared memory until the tile is stable, writes it back and raises a device flag if anything
-// changed; the host relaunches until a launch changes nothing.  One launch advances a front across a
-// whole tile instead of one pixel.  `recon_step_kernel` is the plain Jacobi step, used when the caller
+// same fixed point.  `full_tile_solve` exploits that: a CTA loads a tile plus halo, iterates it in
+// shared memory until the tile is stable, writes it back and asks for its neighbours to run again if
+// anything changed (recon_persist.cuh runs that worklist in one launch).  One tile run advances a front
+// across a whole tile instead of one pixel.  `recon_step_kernel` is the plain Jacobi step, used when the caller
 // bounds the iteration count (max_iter), whose outcome depends on the reference's exact schedule.
 #pragma once
 
 #include "common.cuh"
 
+#include <type_traits>
+
 namespace serron {
 
 constexpr int kRecTile = 64;     // recon tile: 64 x 64 pixels, 256 threads, 16 pixels per thread
 constexpr int kRecThreads = 256;
+
+// A load that bypasses L1 (ld.global.cg): pixels another CTA may have written during this launch.
+template <typename T>
+__device__ __forceinline__ T load_cg(const T* p) {
+    if constexpr (std::is_same<T, __half>::value) {
+        return __ushort_as_half(__ldcg(reinterpret_cast<const unsigned short*>(p)));
+    } else if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+        return __ushort_as_bfloat16(__ldcg(reinterpret_cast<const unsigned short*>(p)));
+    } else {
+        return __ldcg(p);
+    }
+}
 
 template <int OP>
 struct Clip;  // the clip against the mask that follows a step
@@ -63,28 +77,23 @@ __global__ void recon_init_kernel(const T* __restrict__ marker, const T* __restr
     y[i] = Storage<T>::store(Clip<OP>::apply(a, m));
 }
 
-// With `dirty_in`, a launch runs only the tiles flagged in it, and a tile that changed flags its eight
-// neighbours (and itself, if its inner iterations ran out) in `dirty_out`.  Two arrays, swapped and
-// cleared by the host between launches: a tile that read a neighbour's halo while the neighbour was
-// still changing it is flagged for the next launch, which sees the neighbour's final writes.
-// flags[0] is raised whenever a flag is set; the host stops when a launch sets none.  Without
-// `dirty_in` every tile runs and flags[0] says whether anything changed.
+// Full-step tile: solves tile b (tiles numbered plane by plane, row-major within a plane) in shared
+// memory with the step itself, writes it back if it changed, and returns the neighbours to run again
+// as bits 3 * (dy + 1) + (dx + 1): all eight when anything changed, bit 4 (this tile) when its inner
+// iterations ran out.  y is read through L2 (the persistent driver runs a tile on whichever CTA pops
+// it).
 template <typename T, int OP>
-__global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__ y, const T* __restrict__ mask,
-                                                                 const T* __restrict__ w, int C, int H, int W, int kH,
-                                                                 int kW, int kcs, int border, int tiles_x,
-                                                                 int tiles_y, int max_inner, int* __restrict__ flags,
-                                                                 const uint8_t* __restrict__ dirty_in,
-                                                                 uint8_t* __restrict__ dirty_out) {
+__device__ __forceinline__ unsigned full_tile_solve(long long b, T* __restrict__ y, const T* __restrict__ mask,
+                                                    const T* __restrict__ w, int C, int H, int W, int kH, int kW,
+                                                    int kcs, int border, int tiles_x, int tiles_y, int max_inner,
+                                                    unsigned char* smem_raw) {
     using A = typename Storage<T>::acc;
-    extern __shared__ __align__(16) unsigned char smem_raw[];
     const int aH = kH / 2, aW = kW / 2;
     const int sw = kRecTile + kW - 1, sh = kRecTile + kH - 1;
     A* ys = reinterpret_cast<A*>(smem_raw);       // [sh][sw] current values with halo
     A* ms = ys + sw * sh;                          // [TILE][TILE] mask
     A* ws = ms + kRecTile * kRecTile;              // [kH*kW]
 
-    const long long b = blockIdx.x;
     const int tx = static_cast<int>(b % tiles_x), ty = static_cast<int>((b / tiles_x) % tiles_y);
     const long long plane = b / (static_cast<long long>(tiles_x) * tiles_y);
     const int c = static_cast<int>(plane % C);
@@ -95,13 +104,13 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
     const int tid = threadIdx.x;
     const A neutral = Op<OP>::template neutral<A>();
 
-    if (dirty_in && !dirty_in[b]) return;  // one byte, read alike by every thread
     for (int i = tid; i < kH * kW; i += kRecThreads) ws[i] = Storage<T>::load(wc[i]);
     for (int i = tid; i < sw * sh; i += kRecThreads) {
         const int r = i / sw, q = i - r * sw;
         int gr = h0 - aH + r, gq = w0 - aW + q;
         A v = neutral;
-        if (resolve(gr, H, border) && resolve(gq, W, border)) v = Storage<T>::load(yp[static_cast<long long>(gr) * W + gq]);
+        if (resolve(gr, H, border) && resolve(gq, W, border))
+            v = Storage<T>::load(load_cg(yp + static_cast<long long>(gr) * W + gq));
         ys[i] = v;
     }
     for (int i = tid; i < kRecTile * kRecTile; i += kRecThreads) {
@@ -121,7 +130,7 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
         if (sr < 0 || sr >= sh || sq < 0 || sq >= sw) {
             // a window folded from beyond the staged halo (REFLECT on an image narrower than the
             // window): read the current global value; a stale value only delays convergence
-            s = Storage<T>::load(yp[static_cast<long long>(gr) * W + gq]);
+            s = Storage<T>::load(load_cg(yp + static_cast<long long>(gr) * W + gq));
             return true;
         }
         s = ys[sr * sw + sq];
@@ -151,22 +160,14 @@ __global__ void __launch_bounds__(kRecThreads) recon_tile_kernel(T* __restrict__
         }
         any_change = true;
     }
-    if (any_change) {
-        for (int i = tid; i < kRecTile * kRecTile; i += kRecThreads) {
-            const int lr = i / kRecTile, lq = i - lr * kRecTile;
-            const int gr = h0 + lr, gq = w0 + lq;
-            if (gr < H && gq < W) yp[static_cast<long long>(gr) * W + gq] = Storage<T>::store(ys[(lr + aH) * sw + lq + aW]);
-        }
-        if (dirty_in) {
-            // the neighbours, and the tile itself when its inner iterations ran out before it settled
-            if (tid < 9 && (tid != 4 || !settled)) {
-                const int nx = tx + tid % 3 - 1, ny = ty + tid / 3 - 1;
-                if (nx >= 0 && nx < tiles_x && ny >= 0 && ny < tiles_y)
-                    dirty_out[plane * tiles_x * tiles_y + static_cast<long long>(ny) * tiles_x + nx] = 1;
-            }
-        }
-        if (tid == 0) atomicOr(flags, 1);
+    if (!any_change) return 0u;
+    for (int i = tid; i < kRecTile * kRecTile; i += kRecThreads) {
+        const int lr = i / kRecTile, lq = i - lr * kRecTile;
+        const int gr = h0 + lr, gq = w0 + lq;
+        if (gr < H && gq < W) yp[static_cast<long long>(gr) * W + gq] = Storage<T>::store(ys[(lr + aH) * sw + lq + aW]);
     }
+    // the eight neighbours, and the tile itself when its inner iterations ran out before it settled
+    return 0x1efu | (settled ? 0u : 0x10u);
 }
 
 // One Jacobi step y_out = clip(op(y_in), mask); changed[0] |= any pixel differs from y_in.

@@ -315,27 +315,27 @@ __global__ void __launch_bounds__(kScanThreads) recon_cols_kernel(T* __restrict_
 // four line taps) and an in-place pass of the diagonal taps, until none changes anything.  Four threads share a row (or a column), 16 pixels each: each
 // composes its run's clamps, the four runs are scanned with shuffles, then applied.  Halo cells outside
 // the image hold the neutral element (a border tap is left to the opposite scan, which reads the same
-// pixel).  A tile that changed a pixel on an edge flags the neighbour across that edge in
-// `dirty_out`; the launch runs the tiles flagged in `dirty_in` (recon_tile_kernel states why two).
+// pixel).  A tile that changed a pixel on an edge asks for the neighbour across that edge to run again
+// (recon_persist.cuh runs the worklist).
 constexpr int kScanTile = 64;
 constexpr int kScanTileThreads = 256;                           // four threads per line
 constexpr int kLineLanes = kScanTileThreads / kScanTile, kLineRun = kScanTile / kLineLanes;
 template <typename A>
 constexpr size_t scan_tile_smem() { return static_cast<size_t>((kScanTile + 2) + kScanTile) * (kScanTile + 3) * sizeof(A); }
 
+// Solves tile b (tiles numbered plane by plane, row-major within a plane) in shared memory, writes it
+// back if it changed, and returns the neighbours to run again as bits 3 * (dy + 1) + (dx + 1) (bit 4:
+// this tile, when its inner iterations ran out).  y is read through L2: the persistent driver runs a
+// tile on whichever CTA pops it.
 template <typename T, int OP>
-__global__ void __launch_bounds__(kScanTileThreads, 6) recon_tile_scan_kernel(T* __restrict__ y, const T* __restrict__ mask, int H,
-                                                              int W, int tiles_x, int tiles_y, int cls, int max_inner,
-                                                              int* __restrict__ flags,
-                                                              const uint8_t* __restrict__ dirty_in,
-                                                              uint8_t* __restrict__ dirty_out) {
+__device__ __forceinline__ unsigned scan_tile_solve(long long b, T* __restrict__ y, const T* __restrict__ mask, int H,
+                                                    int W, int tiles_x, int tiles_y, int cls, int max_inner,
+                                                    unsigned char* smem_raw) {
     using A = typename Storage<T>::acc;
     using R = ReconClamp<OP>;
     constexpr int TS = kScanTile, P = TS + 3;  // pitch: odd
-    extern __shared__ __align__(16) unsigned char smem_raw[];
     A* ys = reinterpret_cast<A*>(smem_raw);  // [TS + 2][P], pixel (r, c) of the tile at (r + 1, c + 1)
     A* ms = ys + (TS + 2) * P;                // [TS][P]
-    const long long b = blockIdx.x;
     const int tx = static_cast<int>(b % tiles_x), ty = static_cast<int>((b / tiles_x) % tiles_y);
     const long long plane = b / (static_cast<long long>(tiles_x) * tiles_y);
     const int h0 = ty * TS, w0 = tx * TS;
@@ -345,14 +345,13 @@ __global__ void __launch_bounds__(kScanTileThreads, 6) recon_tile_scan_kernel(T*
     const A idp = Op<OP>::template neutral<A>();
     const A idq = Op<OP == kDilate ? kErode : kDilate>::template neutral<A>();
 
-    if (!dirty_in[b]) return;  // one byte, read alike by every thread
     const int th = min(TS, H - h0), tw = min(TS, W - w0);
     for (int i = tid; i < (TS + 2) * (TS + 2); i += kScanTileThreads) {
         const int r = i / (TS + 2), q = i - r * (TS + 2);
         const int gr = h0 + r - 1, gq = w0 + q - 1;
         A v = idp;
         if (gr >= 0 && gr < H && gq >= 0 && gq < W && r <= th + 1 && q <= tw + 1)
-            v = Storage<T>::load(yp[static_cast<long long>(gr) * W + gq]);
+            v = Storage<T>::load(load_cg(yp + static_cast<long long>(gr) * W + gq));
         ys[r * P + q] = v;
     }
     for (int i = tid; i < TS * TS; i += kScanTileThreads) {
@@ -487,7 +486,7 @@ __global__ void __launch_bounds__(kScanTileThreads, 6) recon_tile_scan_kernel(T*
         }
         any = true;
     }
-    if (!any) return;
+    if (!any) return 0u;
     for (int i = tid; i < th * tw; i += kScanTileThreads) {
         const int r = i / tw, q = i - r * tw;
         yp[static_cast<long long>(h0 + r) * W + w0 + q] = Storage<T>::store(ys[(r + 1) * P + q + 1]);
@@ -499,25 +498,12 @@ __global__ void __launch_bounds__(kScanTileThreads, 6) recon_tile_scan_kernel(T*
     __syncthreads();
     if (edges) atomicOr(&edge_s, edges);
     __syncthreads();
-    if (tid < 9) {
-        const int e = edge_s;
-        const bool diag = cls & kScanDiag;
-        int nx = tx, ny = ty;
-        bool go = false;
-        if (tid == 0) { ny = ty - 1; go = e & 1; }
-        if (tid == 1) { ny = ty + 1; go = e & 2; }
-        if (tid == 2) { nx = tx - 1; go = e & 4; }
-        if (tid == 3) { nx = tx + 1; go = e & 8; }
-        if (tid == 4) go = !settled;
-        if (tid == 5) { nx = tx - 1; ny = ty - 1; go = diag && (e & 16); }
-        if (tid == 6) { nx = tx + 1; ny = ty - 1; go = diag && (e & 32); }
-        if (tid == 7) { nx = tx - 1; ny = ty + 1; go = diag && (e & 64); }
-        if (tid == 8) { nx = tx + 1; ny = ty + 1; go = diag && (e & 128); }
-        if (go && nx >= 0 && nx < tiles_x && ny >= 0 && ny < tiles_y) {
-            dirty_out[plane * tiles_x * tiles_y + static_cast<long long>(ny) * tiles_x + nx] = 1;
-            atomicOr(flags, 1);
-        }
-    }
+    const int e = edge_s;
+    unsigned bits = (e & 1 ? 1u << 1 : 0u) | (e & 2 ? 1u << 7 : 0u) | (e & 4 ? 1u << 3 : 0u) | (e & 8 ? 1u << 5 : 0u) |
+                    (settled ? 0u : 1u << 4);
+    if (cls & kScanDiag)
+        bits |= (e & 16 ? 1u << 0 : 0u) | (e & 32 ? 1u << 2 : 0u) | (e & 64 ? 1u << 6 : 0u) | (e & 128 ? 1u << 8 : 0u);
+    return bits;
 }
 
 }  // namespace serron

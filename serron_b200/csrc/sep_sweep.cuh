@@ -11,9 +11,13 @@
 //   column pass  the same over the row results.
 // With a winner buffer every output gets the direct tap di * K + dj of its winner (di from the column
 // pass, dj from the row pass of the winning row), the record the direct kernels write.
+// Compare-selects keep the first extremum (the reference's tie rule); NaN samples enter as the
+// neutral element, so they never win.
 #pragma once
 
 #include "common.cuh"
+
+#include <type_traits>
 
 namespace serron {
 
@@ -27,6 +31,8 @@ __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gmem_src) 
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all_but_one() { asm volatile("cp.async.wait_group 1;\n" ::: "memory"); }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_group 0;\n" ::: "memory"); }
+
+constexpr int kSweepMarkPitch = 128;  // mark bytes per buffer row: image columns [ow0 - 32, ow0 + 96)
 
 template <int K, int ELEM>
 struct SweepGeom {
@@ -42,11 +48,12 @@ struct SweepGeom {
     static constexpr int NCC = TH / K;                   // column-pass chunks per column
     static constexpr size_t XS_BYTES = ((size_t(TH) * XS * ELEM + 15) / 16) * 16;
     static constexpr size_t RD_END = ((2 * XS_BYTES + size_t(RR) * RS * 4 + size_t(RR) * RS) + 15) / 16 * 16;
-    static constexpr int QCAP = 32 * K;  // winner-cell queue of a warp: one task's pushes at most
-    static constexpr size_t QUEUE_BYTES = size_t(kSweepThreads / 32) * QCAP * 2;
-    // the queues live in the step's staging buffer, dead once its row pass is done, where they fit
-    static constexpr bool QUEUE_IN_STAGE = XS_BYTES >= QUEUE_BYTES;
-    static constexpr size_t fwd_smem() { return RD_END + (QUEUE_IN_STAGE ? 0 : QUEUE_BYTES); }
+    // winner marks of one step, a byte per pixel of the buffer rows; they live in the step's staging
+    // buffer, dead once its row pass is done, where they fit
+    static constexpr size_t MARK_BYTES = size_t(RR) * kSweepMarkPitch;
+    static constexpr bool MARK_IN_STAGE = XS_BYTES >= MARK_BYTES;
+    static constexpr int MARK_ROWS_IN_STAGE = int((MARK_BYTES + size_t(XS) * ELEM - 1) / (size_t(XS) * ELEM));
+    static constexpr size_t fwd_smem() { return RD_END + (MARK_IN_STAGE ? 0 : MARK_BYTES); }
 };
 
 // One run of K windows [m, m+K-1], m = 0..K-1, over samples v[0..2K-2]: value and first-extremum
@@ -82,17 +89,28 @@ __device__ __forceinline__ void sweep_run(const float (&v)[2 * K - 1], Emit emit
     }
 }
 
-template <typename T>
-__device__ __forceinline__ float load_clean(T v, float neutral) {
+// NaN never wins: it becomes the neutral element (max / min against the neutral element ignores a NaN
+// operand and returns every other value, -0.0 included, unchanged).
+template <int OP, typename T>
+__device__ __forceinline__ float load_clean(T v) {
     const float f = Storage<T>::load(v);
-    return f != f ? neutral : f;  // NaN never wins: staged as the neutral element
+    return OP == kDilate ? fmaxf(f, __int_as_float(0xff800000)) : fminf(f, __int_as_float(0x7f800000));
+}
+
+// 32 mark bytes (each 0 or 1) as the bits of one word, byte i -> bit i.
+__device__ __forceinline__ uint32_t pack_marks(uint4 lo, uint4 hi) {
+    const uint32_t q[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+    uint32_t bits = 0;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bits |= ((q[e] | (q[e] >> 7) | (q[e] >> 14) | (q[e] >> 21)) & 0xfu) << (4 * e);
+    return bits;
 }
 
 // With `map` (records only), every winner is also set in the target map of the gather (one bit per
-// pixel, rows of ceil(W / 32) words, zero on entry).  In the column pass a lane whose winning row
-// result differs from the one of the output above pushes it to its warp's queue (ballot + popc: only
-// the few changes take a slot); the warp then decodes its queue densely into winner pixels and ORs
-// each into the map, skipping one equal to its queue neighbour's.
+// pixel, rows of ceil(W / 32) words, zero on entry).  The column pass marks the winning pixel of each
+// output with a byte in a step-local window of the buffer rows (image columns [ow0 - 32, ow0 + 96));
+// after the pass, each 32-byte run of marks leaves as one word ORed into the map (words across the image
+// edge bit by bit, through the border's folding).
 template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX, int K>
 __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                                       I* __restrict__ win, uint32_t* __restrict__ map,
@@ -100,14 +118,14 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
                                                                       int seg_h) {
     static_assert(K <= 255, "dj is a byte");
     using G = SweepGeom<K, sizeof(T)>;
-    constexpr int a = G::a, TH = G::TH, Cc = G::Cc, XS = G::XS, RS = G::RS;
+    constexpr int a = G::a, TH = G::TH, Cc = G::Cc, XS = G::XS, RS = G::RS, NCR = G::NCR, NCC = G::NCC;
+    constexpr int RR = G::RR, MP = kSweepMarkPitch;
     constexpr bool ASYNC = sizeof(T) == 4;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     T* const xsb0 = reinterpret_cast<T*>(smem_raw);
     T* const xsb1 = reinterpret_cast<T*>(smem_raw + G::XS_BYTES);
     float* rv = reinterpret_cast<float*>(smem_raw + 2 * G::XS_BYTES);   // [RR][RS]
-    uint8_t* rdj = reinterpret_cast<uint8_t*>(rv + G::RR * RS);         // [RR][RS]
-    uint16_t* const queue_own = reinterpret_cast<uint16_t*>(smem_raw + G::RD_END) + (threadIdx.x >> 5) * G::QCAP;
+    uint8_t* rdj = reinterpret_cast<uint8_t*>(rv + RR * RS);             // [RR][RS]
 
     const long long b = blockIdx.x;
     const int strip = static_cast<int>(b % strips);
@@ -131,20 +149,29 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
             int gr = r0 + r;
             T* dst = buf + r * XS;
             if (!resolve(gr, H, border)) {  // a CONSTANT row outside the image: all neutral
-                for (int q = lane; q < Cc; q += 32) dst[q] = neutral_t;
+#pragma unroll
+                for (int q0 = 0; q0 < Cc; q0 += 32)
+                    if (q0 + lane < Cc) dst[q0 + lane] = neutral_t;
                 continue;
             }
             const T* row = xp + static_cast<long long>(gr) * W;
             if (cols_inside) {
                 const T* src = row + (ow0 - a);
-                for (int q = lane; q < Cc; q += 32) {
-                    if constexpr (ASYNC)
-                        cp_async4(dst + q, src + q);
-                    else
-                        dst[q] = src[q];
+#pragma unroll
+                for (int q0 = 0; q0 < Cc; q0 += 32) {
+                    const int q = q0 + lane;
+                    if (q < Cc) {
+                        if constexpr (ASYNC)
+                            cp_async4(dst + q, src + q);
+                        else
+                            dst[q] = src[q];
+                    }
                 }
             } else {
-                for (int q = lane; q < Cc; q += 32) {
+#pragma unroll
+                for (int q0 = 0; q0 < Cc; q0 += 32) {
+                    const int q = q0 + lane;
+                    if (q >= Cc) continue;
                     int gq = ow0 - a + q;
                     if (resolve(gq, W, border)) {
                         if constexpr (ASYNC)
@@ -158,15 +185,17 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
             }
         }
     };
-    // row pass over buffer rows [0, nrows) -> row results rows [dst0, dst0 + nrows); every chunk is
-    // whole (the padding columns hold the neutral element), so no bounds checks
-    auto row_pass = [&](const T* buf, int nrows, int dst0) {
-        for (int task = tid; task < G::NCR * nrows; task += kSweepThreads) {
-            const int c = task / nrows, r = task - c * nrows;
+    // row pass over buffer rows [0, NR) -> row results rows [dst0, dst0 + NR); every chunk is whole (the
+    // padding columns hold the neutral element), so no bounds checks
+    auto row_pass = [&](const T* buf, int dst0, auto nr) {
+        constexpr int NR = decltype(nr)::value;
+#pragma unroll 1
+        for (int task = tid; task < NCR * NR; task += kSweepThreads) {
+            const int c = task / NR, r = task - c * NR;
             const T* src = buf + r * XS + c * K;
             float v[2 * K - 1];
 #pragma unroll
-            for (int m = 0; m < 2 * K - 1; ++m) v[m] = load_clean(src[m], neutral);
+            for (int m = 0; m < 2 * K - 1; ++m) v[m] = load_clean<OP>(src[m]);
             float* rvr = rv + (dst0 + r) * RS + c * K;
             uint8_t* rdr = rdj + (dst0 + r) * RS + c * K;
             sweep_run<K, OP, true>(v, [&](int m, float val, int off) {
@@ -177,7 +206,7 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
     };
 
     // the padding columns of both staging buffers are never staged: neutral once (and again after a step
-    // whose winner queues lived in the buffer)
+    // whose marks lived in the buffer)
     for (int i = tid; i < 2 * TH * (XS - Cc); i += kSweepThreads) {
         const int r = i / (XS - Cc), q = Cc + i % (XS - Cc);
         (r < TH ? xsb0 : xsb1)[(r % TH) * XS + q] = neutral_t;
@@ -192,15 +221,15 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
         cp_async_wait_all_but_one();
     }
     __syncthreads();
-    row_pass(xsb0, K - 1, 0);
+    row_pass(xsb0, 0, std::integral_constant<int, K - 1>{});
 
     int step = 0;
     for (int s0 = oh_begin; s0 < oh_end; s0 += TH, ++step) {
         T* cur = (step & 1) ? xsb0 : xsb1;
         T* nxt = (step & 1) ? xsb1 : xsb0;
         // (the next step's rows go to nxt, and cur is restaged only two steps on, after barriers)
-        uint16_t* const queue =
-            G::QUEUE_IN_STAGE ? reinterpret_cast<uint16_t*>(cur) + (threadIdx.x >> 5) * G::QCAP : queue_own;
+        uint8_t* const marks =
+            G::MARK_IN_STAGE ? reinterpret_cast<uint8_t*>(cur) : smem_raw + G::RD_END;  // [RR][MP]
         __syncthreads();  // nxt is no longer read
         if constexpr (ASYNC) {
             if (s0 + TH < oh_end) stage(nxt, s0 + TH - a + K - 1, TH);
@@ -210,14 +239,18 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
             stage(cur, s0 - a + K - 1, TH);
         }
         __syncthreads();
-        row_pass(cur, TH, K - 1);
+        row_pass(cur, K - 1, std::integral_constant<int, TH>{});
         __syncthreads();
+        if (marking) {  // cur is dead: its bytes become this step's marks
+            for (int i = tid; i < int(G::MARK_BYTES / 16); i += kSweepThreads)
+                reinterpret_cast<uint4*>(marks)[i] = make_uint4(0, 0, 0, 0);
+            __syncthreads();
+        }
 
         // column pass: output row s0 + i uses row results [i, i + K - 1]
         const int rows_left = oh_end - s0;  // >= TH except in a segment's last step
-        // (the task count is a multiple of 32, so every warp runs whole: lanes past the image edge stay in
-        // the loop with nothing to write, and the winner de-duplication below can shuffle across the warp)
-        for (int task = tid; task < G::NCC * kSweepTW; task += kSweepThreads) {
+#pragma unroll 1
+        for (int task = tid; task < NCC * kSweepTW; task += kSweepThreads) {
             const int c = task / kSweepTW, j = task - c * kSweepTW;
             const int base = c * K;
             const int ow = ow0 + j;
@@ -231,7 +264,7 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
             T* yp = y + plane * H * W;
             I* wp = win + plane * H * W;
             const uint8_t* dj_col = rdj + base * RS + j;
-            int qn = 0, prev = -1;  // queue length (warp-uniform), this lane's last pushed row result
+            uint8_t* mark_col = marks + base * MP + (32 - a) + j;
             sweep_run<K, OP, WITH_INDEX>(v, [&](int m, float val, int off) {
                 const bool out_ok = col_ok && base + m < rows_left;
                 const int o = o0 + m * W;
@@ -239,43 +272,43 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
                 if (WITH_INDEX && out_ok) {
                     // winning row base + m + off, and the column its own row pass chose
                     const uint32_t djb = dj_col[(m + off) * RS];
-                    wp[o] = static_cast<I>(val == neutral ? IndexTraits<I>::none : static_cast<uint32_t>(off * K) + djb);
-                }
-                if (marking) {
-                    const int cell = out_ok && val != neutral ? base + m + off : -1;
-                    const bool push = cell >= 0 && cell != prev;
-                    prev = cell;
-                    const unsigned bal = __ballot_sync(0xffffffffu, push);
-                    if (push) queue[qn + __popc(bal & ((1u << lane) - 1u))] = static_cast<uint16_t>(cell * kSweepTW + j);
-                    qn += __popc(bal);
+                    const bool none = val == neutral;
+                    wp[o] = static_cast<I>(none ? IndexTraits<I>::none : static_cast<uint32_t>(off * K) + djb);
+                    if (marking && !none) mark_col[(m + off) * MP + djb] = 1;
                 }
             });
-            if (marking) {
-                // the queued row results' winners (row s0 - a + i, column ow0 + j - a + dj, border folded)
-                __syncwarp();
-                for (int q0 = 0; q0 < qn; q0 += 32) {
-                    int key = -1, wx = 0, wy = 0;
-                    if (q0 + lane < qn) {
-                        const int e = queue[q0 + lane];
-                        const int i = e / kSweepTW, jj = e - i * kSweepTW;
-                        wx = s0 - a + i;
-                        wy = ow0 + jj - a + static_cast<int>(rdj[i * RS + jj]);
-                        if ((static_cast<unsigned>(wx) < static_cast<unsigned>(H) || resolve(wx, H, border)) &&
-                            (static_cast<unsigned>(wy) < static_cast<unsigned>(W) || resolve(wy, W, border)))
-                            key = wx * W + wy;  // < H * W < 2^31
-                    }
-                    const int left = __shfl_up_sync(0xffffffffu, key, 1);
-                    if (key >= 0 && (lane == 0 || left != key))
-                        atomicOr(&map[(plane * H + wx) * WW + (wy >> 5)], 1u << (wy & 31));
-                }
-                __syncwarp();  // the queue is refilled by the warp's next task
-            }
         }
         __syncthreads();
-        // the queues overwrote cur: its padding columns back to neutral before its next row pass
-        if (G::QUEUE_IN_STAGE && marking)
-            for (int i = tid; i < TH * (XS - Cc); i += kSweepThreads)
-                cur[(i / (XS - Cc)) * XS + Cc + i % (XS - Cc)] = neutral_t;
+        if (marking) {
+            // the marks of buffer rows (image rows s0 - a + i) leave as map words; words and rows inside
+            // the image whole, the others bit by bit through the border's folding.  Rows a later step
+            // marks again (the carried ones) are ORed again then.
+            const long long map_plane = plane * H;
+#pragma unroll 1
+            for (int t = tid; t < RR * (MP / 32); t += kSweepThreads) {
+                const int i = t / (MP / 32), k = t - i * (MP / 32);
+                const uint4* src = reinterpret_cast<const uint4*>(marks + i * MP + 32 * k);
+                const uint32_t bits = pack_marks(src[0], src[1]);
+                if (bits == 0u) continue;
+                const int gr = s0 - a + i, gc0 = ow0 - 32 + 32 * k;
+                if (gr >= 0 && gr < H && gc0 >= 0 && gc0 + 32 <= W) {
+                    atomicOr(&map[(map_plane + gr) * WW + (gc0 >> 5)], bits);
+                } else {
+                    for (uint32_t m = bits; m; m &= m - 1) {
+                        int r = gr, cc = gc0 + __ffs(m) - 1;
+                        if (resolve(r, H, border) && resolve(cc, W, border))
+                            atomicOr(&map[(map_plane + r) * WW + (cc >> 5)], 1u << (cc & 31));
+                    }
+                }
+            }
+            // the marks overwrote cur's padding columns: neutral again before its next row pass (once
+            // every mark is read)
+            if constexpr (G::MARK_IN_STAGE) {
+                __syncthreads();
+                for (int i = tid; i < G::MARK_ROWS_IN_STAGE * (XS - Cc); i += kSweepThreads)
+                    cur[(i / (XS - Cc)) * XS + Cc + i % (XS - Cc)] = neutral_t;
+            }
+        }
         // carry the last K-1 row results to the top
         for (int i = tid; i < (K - 1) * RS; i += kSweepThreads) {
             rv[i] = rv[TH * RS + i];

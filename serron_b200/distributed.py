@@ -8,9 +8,10 @@ The reference is single-process; this module adds the two ways the morphology pa
   run-to-run identical result (all-gather of the per-rank gradients, then a fixed-order local sum).
 * **Row (H) sharding of one reconstruction** — :func:`reconstruction_sharded` keeps each rank's block
   of rows plus a halo of ``kH // 2`` rows above and ``kH - 1 - kH // 2`` below.  Each round every rank
-  solves its block to a local fixed point with the halo rows frozen at the neighbours' current values
-  (their marker and mask are both set to those values, so the clipped step cannot move them), then
-  the ranks exchange their boundary rows and all-reduce a "changed" flag.  A round in which no rank
+  receives its halo rows from its two neighbours only (point-to-point sends into local buffers), solves
+  its block to a local fixed point with the halo frozen at those values (their marker and mask are both
+  set to them, so the clipped step cannot move them), and the ranks all-reduce a "changed" flag that is
+  computed on the device (one host read per round).  A round in which no rank
   changed anything ends the loop: every block then satisfies the fixed-point equation against its
   neighbours' final rows, so the union is the global fixed point, bit-identical to the single-GPU
   result (the step is monotone; every schedule converges to the same least fixed point).
@@ -115,32 +116,41 @@ def reconstruction_sharded(marker: torch.Tensor, mask: torch.Tensor, kernel: tor
     n, c, h, w = current.shape
     if (rank > 0 and h < bot_h) or (rank < world - 1 and h < top_h):
         raise ValueError("reconstruction_sharded: each block needs at least as many rows as the halo")
+    up = rank - 1 if rank > 0 else None          # the rank holding the rows above
+    down = rank + 1 if rank < world - 1 else None  # the rows below
+    peer = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
+    halo_above = current.new_empty((n, c, top_h, w)) if up is not None else None
+    halo_below = current.new_empty((n, c, bot_h, w)) if down is not None else None
+    lo = top_h if up is not None else 0
 
     rounds = 0
     while True:
-        # boundary rows of every rank: my first bot_h rows feed the rank above, my last top_h the rank below
-        edge = torch.cat([current[:, :, :bot_h], current[:, :, h - top_h:]], dim=2).contiguous()
-        edges = [torch.empty_like(edge) for _ in range(world)]
-        dist.all_gather(edges, edge, group=group)
-        parts_m, parts_k = [], []
-        above = edges[rank - 1][:, :, bot_h:] if rank > 0 else None   # last top_h rows of the rank above
-        below = edges[rank + 1][:, :, :bot_h] if rank < world - 1 else None  # first bot_h rows of the rank below
-        if above is not None:
-            parts_m.append(above)
-            parts_k.append(above)
-        parts_m.append(current)
-        parts_k.append(mask)
-        if below is not None:
-            parts_m.append(below)
-            parts_k.append(below)
+        # halo rows from the two neighbours only, into local buffers: my first bot_h rows go up (they are
+        # the rows below the rank above), my last top_h rows go down
+        ops = []
+        if up is not None:
+            ops.append(dist.P2POp(dist.irecv, halo_above, peer(up), group))
+            if bot_h:
+                ops.append(dist.P2POp(dist.isend, current[:, :, :bot_h].contiguous(), peer(up), group))
+        if down is not None:
+            ops.append(dist.P2POp(dist.irecv, halo_below, peer(down), group))
+            if top_h:
+                ops.append(dist.P2POp(dist.isend, current[:, :, h - top_h:].contiguous(), peer(down), group))
+        ops = [op for op in ops if op.tensor.numel() > 0]
+        if ops:
+            for req in dist.batch_isend_irecv(ops):
+                req.wait()
+        # frozen halo rows: marker and mask both hold the neighbours' values, so the clipped step keeps them
+        parts_m = ([halo_above] if up is not None else []) + [current] + ([halo_below] if down is not None else [])
+        parts_k = ([halo_above] if up is not None else []) + [mask] + ([halo_below] if down is not None else [])
         ext_marker = torch.cat(parts_m, dim=2).contiguous()
         ext_mask = torch.cat(parts_k, dim=2).contiguous()
         solved = solver(dilate, ext_marker, ext_mask, kernel, border_int)
-        lo = above.shape[2] if above is not None else 0
-        new = solved[:, :, lo:lo + h]
-        changed = torch.tensor([0 if torch.equal(new, current) else 1], dtype=torch.int32, device=current.device)
+        new = solved[:, :, lo:lo + h].contiguous()
+        # the change flag stays on the device until the one read per round, after the all-reduce
+        changed = (new != current).any().to(torch.int32).reshape(1)
         dist.all_reduce(changed, op=dist.ReduceOp.MAX, group=group)
-        current = new.contiguous()
+        current = new
         rounds += 1
         if int(changed.item()) == 0:
             return current

@@ -89,8 +89,15 @@ def test_workspace_sizes_are_deterministic(lib):
     target_map = 32 * 64 * 512 * (512 // 32) * 4  # one bit per pixel
     assert with_w == target_map
     assert without == 32 * 64 * 512 * 512 + target_map  # and one byte per output for the u8 record
-    # relaxation: two dirty bytes per 64x64 tile; the Jacobi schedule: a second image
-    assert lib.serron_reconstruct_workspace_bytes(xs, xd, 0, 0) == 256 + 2 * 32 * 64 * 8 * 8
+    # relaxation: a state word per 64x64 tile and the worklist ring (8 bytes per cell, four cells per tile
+    # plus four per CTA of the largest grid); the Jacobi schedule: a second image
+    tiles = 32 * 64 * 8 * 8
+
+    def align256(v):
+        return (v + 255) // 256 * 256
+
+    assert lib.serron_reconstruct_workspace_bytes(xs, xd, 0, 0) == 256 + align256(4 * tiles) + align256(
+        8 * (4 * tiles + 4 * 4096 + 64))
     assert lib.serron_reconstruct_workspace_bytes(xs, xd, 0, 5) == 256 + 32 * 64 * 512 * 512 * 4
 
 
