@@ -209,6 +209,19 @@ SERRON_API int serron_reconstruct(int32_t dilate, const void* marker, const void
                                   int64_t* steps);
 SERRON_API int64_t serron_reconstruct_workspace_bytes(const int64_t* sizes, int64_t dim, int32_t dtype,
                                                       int64_t max_iter);
+/* Continues a reconstruction whose marker (clipped by the mask) is already at the fixed point except
+ * near the top and bottom edges of each plane: the device worklist starts with only the tiles within
+ * `seed_top` rows of the top and `seed_bottom` rows of the bottom (both >= 0), and any change spreads
+ * from there, to the same fixed point serron_reconstruct reaches.  The halo exchange of a reconstruction
+ * sharded along H calls this after its first round, when only rows next to the received halos can move.
+ * Arguments and workspace as serron_reconstruct with max_iter = 0.  No reference counterpart (the
+ * reference is single-process). */
+SERRON_API int serron_reconstruct_from_edges(int32_t dilate, const void* marker, const void* mask,
+                                             const int64_t* sizes, int64_t dim, const void* kernel,
+                                             const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype,
+                                             int64_t border, int64_t seed_top, int64_t seed_bottom, void* output,
+                                             void* workspace, int64_t workspace_bytes, int32_t device, void* stream,
+                                             int64_t* steps);
 
 /* ---------------------------------------------------------------------------------------------
  * Backward without any allocation.  No counterpart in the reference (its backward allocates its own

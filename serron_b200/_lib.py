@@ -53,6 +53,7 @@ EXPORTED = (
     "serron_backward_static_scratch",
     "serron_winners_bytes",
     "serron_forward_autocast",
+    "serron_reconstruct_from_edges",
 )
 
 
@@ -117,6 +118,9 @@ def load() -> ctypes.CDLL:
         lib.serron_reconstruct.argtypes = [i32, vp, vp, p64, i64, vp, p64, i64, i32, i64, i64, i64, vp, vp, i64, i32,
                                            vp, p64]
         lib.serron_reconstruct.restype = ctypes.c_int
+        lib.serron_reconstruct_from_edges.argtypes = [i32, vp, vp, p64, i64, vp, p64, i64, i32, i64, i64, i64, vp, vp,
+                                                      i64, i32, vp, p64]
+        lib.serron_reconstruct_from_edges.restype = ctypes.c_int
         lib.serron_reconstruct_workspace_bytes.argtypes = [p64, i64, i32, i64]
         lib.serron_reconstruct_workspace_bytes.restype = i64
         lib.serron_backward_static_scratch.argtypes = [i32] + bwd[:14] + [vp, vp, i32, vp]

@@ -3,7 +3,7 @@
 The reference registers eight operators under ``serron::`` (packages/serron/csrc/bindings.cpp:8-19) and
 an autocast rule for the two forwards (packages/serron/torch-ext/serron/_cmake_ops.py:175-189).  This
 module registers the same schemas, implements them for CUDA by calling ``libserron_b200.so`` through
-:mod:`serron_b200._lib`, and registers the same autocast rule.  The CPU key raises: this build has no
+:mod:`serron_b200._lib`, and registers the same autocast rule.  The CPU key raises: this library has no
 CPU path.
 
 The functions below the registrations are what the autograd layer calls directly: they allocate
@@ -206,8 +206,12 @@ def backward_from_winners(op: int, grad_output: torch.Tensor, winners: torch.Ten
 
 
 def reconstruct(dilate: bool, marker: torch.Tensor, mask: torch.Tensor, kernel: torch.Tensor, border: int,
-                max_iter: int | None, check_every: int) -> torch.Tensor:
-    """Geodesic reconstruction on CUDA tensors that already share a dtype and a device."""
+                max_iter: int | None, check_every: int, seed_rows: tuple[int, int] | None = None) -> torch.Tensor:
+    """Geodesic reconstruction on CUDA tensors that already share a dtype and a device.
+
+    ``seed_rows=(top, bottom)``: the marker is already at the fixed point except within ``top`` rows of the
+    top edge and ``bottom`` rows of the bottom edge (``serron_reconstruct_from_edges``; fixed-point mode only).
+    """
     name = "serron.reconstruction_by_dilation" if dilate else "serron.reconstruction_by_erosion"
     _check_tensors(name, marker, kernel)
     m = marker.contiguous()
@@ -221,10 +225,18 @@ def reconstruct(dilate: bool, marker: torch.Tensor, mask: torch.Tensor, kernel: 
     ws_bytes = lib.serron_reconstruct_workspace_bytes(xs, xd, _lib.DTYPE_CODE[m.dtype], mi)
     workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=m.device)
     steps = ctypes.c_int64(0)
-    rc = lib.serron_reconstruct(int(dilate), m.data_ptr(), mk.data_ptr(), xs, xd, k.data_ptr(), ks, kd,
-                                _lib.DTYPE_CODE[m.dtype], int(border), mi, int(check_every), out.data_ptr(),
-                                workspace.data_ptr(), ws_bytes, m.device.index, _lib.stream_of(m),
-                                ctypes.byref(steps))
+    if seed_rows is None:
+        rc = lib.serron_reconstruct(int(dilate), m.data_ptr(), mk.data_ptr(), xs, xd, k.data_ptr(), ks, kd,
+                                    _lib.DTYPE_CODE[m.dtype], int(border), mi, int(check_every), out.data_ptr(),
+                                    workspace.data_ptr(), ws_bytes, m.device.index, _lib.stream_of(m),
+                                    ctypes.byref(steps))
+    else:
+        if mi > 0:
+            raise RuntimeError(f"{name}: an edge-seeded reconstruction runs to the fixed point (max_iter=None)")
+        rc = lib.serron_reconstruct_from_edges(int(dilate), m.data_ptr(), mk.data_ptr(), xs, xd, k.data_ptr(), ks,
+                                               kd, _lib.DTYPE_CODE[m.dtype], int(border), int(seed_rows[0]),
+                                               int(seed_rows[1]), out.data_ptr(), workspace.data_ptr(), ws_bytes,
+                                               m.device.index, _lib.stream_of(m), ctypes.byref(steps))
     _lib.raise_for(rc)
     return out
 

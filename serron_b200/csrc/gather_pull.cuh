@@ -272,10 +272,10 @@ struct SumGeom {
 };
 
 // Sum for one pixel over its KB x KB box (KB = 2a + 1) of one-byte box taps staged in shared memory.
-// The box is unrolled: the taps of a row are matched four at a time against constants, and the
-// matching grad_output loads are issued before the row's additions, which then run back to back in
-// order.
-//   rec      tap row of box row 0 at box column 0 (a byte address; rows rq bytes apart)
+// Box rows run in a loop (the code of one row stays small enough for the instruction cache); within a
+// row the taps are matched four at a time against constants, and the matching grad_output loads are
+// issued before the row's additions, which then run back to back in order.
+//   rec      tap row of box row 0 at box column 0 (a byte address; rows rq bytes apart, rq % 4 == 0)
 //   gp       grad_output of box row 0 at box column 0 (rows gq elements apart)
 //   rows_ok  bit r: box row r lies in the image;  keep[g]: 0x80 in byte k where box column 4g+k does
 template <int KB, typename T>
@@ -285,33 +285,32 @@ __device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed(const uint8_
     using G = typename GradAcc<T>::type;
     constexpr int NG = (KB + 3) / 4;
     G acc = G(0);
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(rec);
+    const uint32_t* row = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
+    const int sh = static_cast<int>(addr & 3) * 8;  // the same in every row: rows are a multiple of 4 bytes apart
+    const int rqw = rq >> 2;
+    // box column j = 4g + k of row r selects the pixel with tap (KB - 1 - r) * KB + (KB - 1) - j: byte k of
+    // group g of row r is matched against pat - (4g * 0x01010101), pat dropping by KB in every byte per row
+    // (bytes past the box may borrow, and are dropped by keep)
+    uint32_t pat = static_cast<uint32_t>((KB - 1) * KB + (KB - 1)) * 0x01010101u - 0x03020100u;
+#pragma unroll 1
+    for (int r = 0; r < KB; ++r, row += rqw, gp += gq, pat -= static_cast<uint32_t>(KB) * 0x01010101u) {
+        if (!(rows_ok & (1u << r))) continue;
+        uint32_t wd[NG + 1];
 #pragma unroll
-    for (int r = 0; r < KB; ++r) {
-        if (rows_ok & (1u << r)) {
-            const uintptr_t addr = reinterpret_cast<uintptr_t>(rec + r * rq);
-            const uint32_t* row = reinterpret_cast<const uint32_t*>(addr & ~uintptr_t(3));
-            const int sh = static_cast<int>(addr & 3) * 8;
-            const T* grow = gp + r * gq;
-            uint32_t wd[NG + 1];
+        for (int i = 0; i <= NG; ++i) wd[i] = row[i];
+        uint32_t m[NG];
 #pragma unroll
-            for (int i = 0; i <= NG; ++i) wd[i] = row[i];
-            uint32_t m[NG];
+        for (int g = 0; g < NG; ++g)
+            m[g] = pg_zero_bytes(__funnelshift_r(wd[g], wd[g + 1], sh) ^ (pat - static_cast<uint32_t>(4 * g) * 0x01010101u)) &
+                   keep[g];
+        G v[KB];
 #pragma unroll
-            for (int g = 0; g < NG; ++g) {
-                // box column j = 4g + k of row r selects the pixel with tap (KB - 1 - r) * KB + (KB - 1) - j;
-                // bytes past the box may borrow, and are dropped by keep
-                const uint32_t pat =
-                    static_cast<uint32_t>((KB - 1 - r) * KB + (KB - 1) - 4 * g) * 0x01010101u - 0x03020100u;
-                m[g] = pg_zero_bytes(__funnelshift_r(wd[g], wd[g + 1], sh) ^ pat) & keep[g];
-            }
-            G v[KB];
+        for (int j = 0; j < KB; ++j)
+            v[j] = (m[j >> 2] >> (8 * (j & 3) + 7)) & 1u ? static_cast<G>(Storage<T>::load(gp[j])) : G(0);
 #pragma unroll
-            for (int j = 0; j < KB; ++j)
-                v[j] = (m[j >> 2] >> (8 * (j & 3) + 7)) & 1u ? static_cast<G>(Storage<T>::load(grow[j])) : G(0);
-#pragma unroll
-            for (int j = 0; j < KB; ++j)
-                if ((m[j >> 2] >> (8 * (j & 3) + 7)) & 1u) acc = GradAcc<T>::add(acc, v[j]);
-        }
+        for (int j = 0; j < KB; ++j)
+            if ((m[j >> 2] >> (8 * (j & 3) + 7)) & 1u) acc = GradAcc<T>::add(acc, v[j]);
     }
     return acc;
 }

@@ -107,19 +107,36 @@ __device__ __forceinline__ int rq_pop(const ReconQueue& q, unsigned long long bu
     }
 }
 
-// Every tile queued once, in order; the rest of the ring cleared (a cell left by an earlier call must
-// not match a slot of this one).
-__global__ void recon_queue_init_kernel(ReconQueue q, int tiles) {
+// The tiles of tile rows [0, row0_end) and [row1_begin, tiles_y) of every plane queued once, in order
+// (all of them when row0_end == tiles_y), the others idle; the rest of the ring cleared (a cell left
+// by an earlier call must not match a slot of this one).  The tail and pending counters start at the
+// number queued.
+__global__ void recon_queue_init_kernel(ReconQueue q, int planes, int tiles_x, int tiles_y, int row0_end,
+                                        int row1_begin) {
     const unsigned int i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (i < static_cast<unsigned int>(tiles)) q.state[i] = kTileQueued;
-    if (i < q.cap)
-        q.cells[i] = i < static_cast<unsigned int>(tiles)
-                         ? (static_cast<unsigned long long>(i + 1) << 32) | i
-                         : 0ull;
+    const int per_plane = tiles_x * tiles_y;
+    const int tiles = planes * per_plane;
+    const int seeded_rows = row0_end + (tiles_y - row1_begin);
+    const int per_plane_seeded = seeded_rows * tiles_x;
+    const unsigned int queued = static_cast<unsigned int>(planes * per_plane_seeded);
+    if (i < static_cast<unsigned int>(tiles)) {
+        const int ty = static_cast<int>(i % per_plane) / tiles_x;
+        q.state[i] = (ty < row0_end || ty >= row1_begin) ? kTileQueued : kTileIdle;
+    }
+    if (i < q.cap) {
+        unsigned long long cell = 0ull;
+        if (i < queued) {
+            const int p = static_cast<int>(i) / per_plane_seeded, rem = static_cast<int>(i) - p * per_plane_seeded;
+            const int sr = rem / tiles_x, tx = rem - sr * tiles_x;
+            const int ty = sr < row0_end ? sr : row1_begin + (sr - row0_end);
+            cell = (static_cast<unsigned long long>(i + 1) << 32) | static_cast<unsigned int>(p * per_plane + ty * tiles_x + tx);
+        }
+        q.cells[i] = cell;
+    }
     if (i == 0) {
         q.counters[0] = 0u;
-        q.counters[1] = static_cast<unsigned int>(tiles);
-        q.counters[2] = static_cast<unsigned int>(tiles);
+        q.counters[1] = queued;
+        q.counters[2] = queued;
         q.counters[3] = 0u;
         q.counters[4] = 0u;
     }

@@ -11,7 +11,9 @@ The reference is single-process; this module adds the two ways the morphology pa
   receives its halo rows from its two neighbours only (point-to-point sends into local buffers), solves
   its block to a local fixed point with the halo frozen at those values (their marker and mask are both
   set to them, so the clipped step cannot move them), and the ranks all-reduce a "changed" flag that is
-  computed on the device (one host read per round).  A round in which no rank
+  computed on the device (one host read per round).  After the first round a block is already at its
+  fixed point for the previous halos, so the library's solver continues from it with its tile worklist
+  seeded only next to the halo rows (``serron_reconstruct_from_edges``).  A round in which no rank
   changed anything ends the loop: every block then satisfies the fixed-point equation against its
   neighbours' final rows, so the union is the global fixed point, bit-identical to the single-GPU
   result (the step is monotone; every schedule converges to the same least fixed point).
@@ -84,11 +86,11 @@ def allreduce_se_grads(params: Iterable[torch.nn.Parameter], *, average: bool = 
 LocalSolver = Callable[[bool, torch.Tensor, torch.Tensor, torch.Tensor, int], torch.Tensor]
 
 
-def _default_solver(dilate: bool, marker: torch.Tensor, mask: torch.Tensor, kernel: torch.Tensor, border: int
-                    ) -> torch.Tensor:
+def _default_solver(dilate: bool, marker: torch.Tensor, mask: torch.Tensor, kernel: torch.Tensor, border: int,
+                    seed_rows: tuple[int, int] | None = None) -> torch.Tensor:
     from . import _ops
 
-    return _ops.reconstruct(dilate, marker, mask, kernel, border, None, 16)
+    return _ops.reconstruct(dilate, marker, mask, kernel, border, None, 16, seed_rows=seed_rows)
 
 
 def reconstruction_sharded(marker: torch.Tensor, mask: torch.Tensor, kernel: torch.Tensor, *, dilate: bool = True,
@@ -106,6 +108,7 @@ def reconstruction_sharded(marker: torch.Tensor, mask: torch.Tensor, kernel: tor
     :returns: this rank's block of the reconstruction.
     :raises RuntimeError: when ``max_rounds`` runs out.
     """
+    library_solver = solver is None  # the library's solver can continue from the previous round's result
     solver = solver or _default_solver
     rank, world = dist.get_rank(group), dist.get_world_size(group)
     kh = kernel.shape[-2]
@@ -119,9 +122,16 @@ def reconstruction_sharded(marker: torch.Tensor, mask: torch.Tensor, kernel: tor
     up = rank - 1 if rank > 0 else None          # the rank holding the rows above
     down = rank + 1 if rank < world - 1 else None  # the rows below
     peer = (lambda r: dist.get_global_rank(group, r)) if group is not None else (lambda r: r)
-    halo_above = current.new_empty((n, c, top_h, w)) if up is not None else None
-    halo_below = current.new_empty((n, c, bot_h, w)) if down is not None else None
-    lo = top_h if up is not None else 0
+    top = top_h if up is not None else 0
+    bot = bot_h if down is not None else 0
+    halo_above = current.new_empty((n, c, top, w))
+    halo_below = current.new_empty((n, c, bot, w))
+    # the block with its halo rows: marker and mask both hold the neighbours' values there (frozen: the
+    # clipped step cannot move them)
+    ext_marker = current.new_empty((n, c, top + h + bot, w))
+    ext_mask = torch.empty_like(ext_marker)
+    ext_marker[:, :, top:top + h] = current
+    ext_mask[:, :, top:top + h] = mask
 
     rounds = 0
     while True:
@@ -130,27 +140,33 @@ def reconstruction_sharded(marker: torch.Tensor, mask: torch.Tensor, kernel: tor
         ops = []
         if up is not None:
             ops.append(dist.P2POp(dist.irecv, halo_above, peer(up), group))
-            if bot_h:
-                ops.append(dist.P2POp(dist.isend, current[:, :, :bot_h].contiguous(), peer(up), group))
+            ops.append(dist.P2POp(dist.isend, current[:, :, :bot_h].contiguous(), peer(up), group))
         if down is not None:
             ops.append(dist.P2POp(dist.irecv, halo_below, peer(down), group))
-            if top_h:
-                ops.append(dist.P2POp(dist.isend, current[:, :, h - top_h:].contiguous(), peer(down), group))
+            ops.append(dist.P2POp(dist.isend, current[:, :, h - top_h:].contiguous(), peer(down), group))
         ops = [op for op in ops if op.tensor.numel() > 0]
         if ops:
             for req in dist.batch_isend_irecv(ops):
                 req.wait()
-        # frozen halo rows: marker and mask both hold the neighbours' values, so the clipped step keeps them
-        parts_m = ([halo_above] if up is not None else []) + [current] + ([halo_below] if down is not None else [])
-        parts_k = ([halo_above] if up is not None else []) + [mask] + ([halo_below] if down is not None else [])
-        ext_marker = torch.cat(parts_m, dim=2).contiguous()
-        ext_mask = torch.cat(parts_k, dim=2).contiguous()
-        solved = solver(dilate, ext_marker, ext_mask, kernel, border_int)
-        new = solved[:, :, lo:lo + h].contiguous()
+        if top:
+            ext_marker[:, :, :top] = halo_above
+            ext_mask[:, :, :top] = halo_above
+        if bot:
+            ext_marker[:, :, top + h:] = halo_below
+            ext_mask[:, :, top + h:] = halo_below
+        if rounds > 0 and library_solver:
+            # the block is at its fixed point for the previous halos: only tiles within reach of the halo
+            # rows can move, and the worklist starts there
+            solved = _default_solver(dilate, ext_marker, ext_mask, kernel, border_int,
+                                     seed_rows=(top + kh if top else 0, bot + kh if bot else 0))
+        else:
+            solved = solver(dilate, ext_marker, ext_mask, kernel, border_int)
+        new = solved[:, :, top:top + h]
         # the change flag stays on the device until the one read per round, after the all-reduce
         changed = (new != current).any().to(torch.int32).reshape(1)
         dist.all_reduce(changed, op=dist.ReduceOp.MAX, group=group)
-        current = new
+        current = new.contiguous()
+        ext_marker = solved
         rounds += 1
         if int(changed.item()) == 0:
             return current

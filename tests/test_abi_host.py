@@ -102,10 +102,11 @@ def test_workspace_sizes_are_deterministic(lib):
 
 
 def test_thresholds_table(lib):
-    assert lib.serron_get_separable_min_k(0, 0, 0) == 11
+    # the B200-measured default (the reference's is 11)
+    assert lib.serron_get_separable_min_k(0, 0, 0) == 3
     assert lib.serron_set_separable_min_k(0, 0, 0, 7) == 7
-    assert lib.serron_get_separable_min_k(0, 0, 1) == 11
-    assert lib.serron_set_separable_min_k(0, 0, 0, 0) == 11
+    assert lib.serron_get_separable_min_k(0, 0, 1) == 3
+    assert lib.serron_set_separable_min_k(0, 0, 0, 0) == 3
 
 
 def test_public_api_surface():

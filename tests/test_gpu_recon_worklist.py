@@ -62,3 +62,33 @@ def test_full_step_tiles_with_a_wide_window(serron):
     want = oracle.reconstruct_flood(True, marker, mask, w, CONSTANT)
     got = serron.reconstruction_by_dilation(marker.cuda(), mask.cuda(), w.cuda(), border=serron.BorderMode.CONSTANT)
     assert torch.equal(got.cpu(), want)
+
+
+@pytest.mark.parametrize("n", [600, 577])  # 577: a last tile row of one pixel row, the seed rows reach the one above
+@pytest.mark.parametrize("kind", ["cross", "square", "diamond"])
+@pytest.mark.parametrize("dilate", [True, False])
+def test_edge_seeded_continuation(serron, kind, dilate, n):
+    """``serron_reconstruct_from_edges``: a marker already at its fixed point except near the top and
+    bottom edges reaches the full reconstruction's result with only the edge tiles queued at first."""
+    from serron_b200 import _ops
+
+    g = torch.Generator().manual_seed(21 + int(dilate))
+    marker, mask = oracle.blob_mask(n, blobs=9, seeds=4, seed=13)
+    if not dilate:  # the dual: marker above the mask, fronts that lower it
+        mask, marker = 1.0 - mask, 1.0 - marker
+    w = getattr(serron.structuring_element, kind)(2 if kind == "diamond" else 3).cuda()  # 5x5, 3x3, 3x3
+    kh = w.shape[-2]
+    # the fixed point of the marker without its edge seeds, then new seeds in the top and bottom 8 rows
+    inner = marker.clone()
+    inner[:, :, :8] = marker.min() if dilate else marker.max()
+    inner[:, :, -8:] = marker.min() if dilate else marker.max()
+    settled = _ops.reconstruct(dilate, inner.cuda(), mask.cuda(), w, 2, None, 16)
+    edge_seeds = torch.rand(1, 1, n, n, generator=g) < 0.02
+    edge_seeds[:, :, 8:-8] = False
+    start = torch.where(edge_seeds.cuda(), mask.cuda(), settled)
+    want = _ops.reconstruct(dilate, start, mask.cuda(), w, 2, None, 16)
+    got = _ops.reconstruct(dilate, start, mask.cuda(), w, 2, None, 16, seed_rows=(8 + kh, 8 + kh))
+    assert torch.equal(got, want)
+    # nothing seeded: the marker is taken as the fixed point it is
+    same = _ops.reconstruct(dilate, want, mask.cuda(), w, 2, None, 16, seed_rows=(0, 0))
+    assert torch.equal(same, want)
