@@ -122,9 +122,6 @@ SERRON_API int serron_forward(int32_t op, const void* input, const int64_t* inpu
                               const void* kernel, const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype,
                               int64_t border, int32_t flat, int64_t algo, void* output, void* winners,
                               int32_t winners_format, int32_t device, void* stream);
-/* Bytes of a record buffer of `winners_format` for an input of `sizes` (4-D): one record per output,
- * plus the target map when the format carries SERRON_WINNERS_MAP; -1 for bad arguments.  No
- * reference counterpart (the reference keeps no winner records). */
 /* The forward under CUDA autocast, with the backward's winners.  Replaces, for the calls it takes, the
  * reference's autocast path: serron::erode/dilate on float16 casts of their arguments
  * (packages/serron/torch-ext/serron/_cmake_ops.py:175-189) followed, in the backward, by a winner search
@@ -139,6 +136,9 @@ SERRON_API int serron_forward_autocast(int32_t op, const void* input, const int6
                                        int64_t kernel_dim, int32_t kernel_dtype, int64_t border, void* output,
                                        void* winners, int32_t winners_format, int32_t device, void* stream);
 
+/* Bytes of a record buffer of `winners_format` for an input of `sizes` (4-D): one record per output,
+ * plus the target map when the format carries SERRON_WINNERS_MAP; -1 for bad arguments.  No
+ * reference counterpart (the reference keeps no winner records). */
 SERRON_API int64_t serron_winners_bytes(const int64_t* sizes, int64_t dim, int32_t winners_format);
 
 /* ---------------------------------------------------------------------------------------------
@@ -174,6 +174,41 @@ SERRON_API int serron_backward_from_winners(int32_t op, const void* grad_output,
 SERRON_API int64_t serron_backward_workspace_bytes(const int64_t* sizes, int64_t dim, const int64_t* kernel_sizes,
                                                    int64_t kernel_dim, int32_t need_kernel_grad,
                                                    int32_t winners_format, int32_t with_winners);
+/* serron_backward_from_winners in float32 arithmetic with grad_output read as `grad_output_dtype` and
+ * grad_input written as `grad_input_dtype` (each float32, float16 or bfloat16; grad_kernel float32):
+ * the same results as widening grad_output to float32, running serron_backward_from_winners with
+ * dtype float32 and rounding grad_input to its dtype (to nearest even), without those two copies.  It
+ * serves the backward that follows serron_forward_autocast, where the reference's autograd casts the
+ * float16 grad_output up to the promoted float32 and the float32 grad_input down to the input's dtype
+ * (packages/serron/torch-ext/serron/autograd.py:37-76).  Direct one- or two-byte records with their
+ * target map only.  Workspace: serron_backward_workspace_bytes(..., with_winners = 1). */
+SERRON_API int serron_backward_from_winners_widened(int32_t op, const void* grad_output, int32_t grad_output_dtype,
+                                                    const int64_t* sizes, int64_t dim, const int64_t* kernel_sizes,
+                                                    int64_t kernel_dim, int64_t border, int32_t need_kernel_grad,
+                                                    const void* winners, int32_t winners_format, void* grad_input,
+                                                    int32_t grad_input_dtype, void* grad_kernel, void* workspace,
+                                                    int64_t workspace_bytes, int32_t device, void* stream);
+
+/* ---------------------------------------------------------------------------------------------
+ * Derived operations in one launch.  Replace, for the calls they take, the reference's compositions
+ * (packages/serron/torch-ext/serron/functional.py:40-92): mode 0 gradient = dilation(x) - erosion(x),
+ * 1 opening = dilation(erosion(x)), 2 closing = erosion(dilation(x)), 3 top_hat = x - opening(x),
+ * 4 black_hat = closing(x) - x, each bit-identical to the composition (the intermediate image rounded to
+ * `dtype` as the reference's intermediate tensor is, the subtraction in `dtype`).  The gradient finds
+ * both extremes over one staged tile; the others keep the intermediate in shared memory.  `winners_a` and
+ * `winners_b` (serron_winners_bytes of SERRON_WINNERS_DIRECT_U8 | SERRON_WINNERS_MAP each) get the direct
+ * records and target maps of the two operations (gradient: a = dilation, b = erosion, both over x;
+ * otherwise a = the first operation over x, b = the second over the intermediate), for
+ * serron_backward_from_winners.  serron_derived_supported says whether a call is taken: both window
+ * sides at most 7 and, for modes 1-4, an image at least as large as the window.  No reference
+ * counterpart.
+ * --------------------------------------------------------------------------------------------- */
+SERRON_API int serron_derived_supported(int32_t mode, const int64_t* input_sizes, int64_t input_dim,
+                                        const int64_t* kernel_sizes, int64_t kernel_dim);
+SERRON_API int serron_derived_forward(int32_t mode, const void* input, const int64_t* input_sizes, int64_t input_dim,
+                                      const void* kernel, const int64_t* kernel_sizes, int64_t kernel_dim,
+                                      int32_t dtype, int64_t border, void* output, void* winners_a, void* winners_b,
+                                      int32_t winners_format, int32_t device, void* stream);
 
 /* ---------------------------------------------------------------------------------------------
  * Algorithm selection.  Replace serron::feasible_algos / heuristic_algo / set_separable_min_k /

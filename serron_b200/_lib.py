@@ -54,6 +54,9 @@ EXPORTED = (
     "serron_winners_bytes",
     "serron_forward_autocast",
     "serron_reconstruct_from_edges",
+    "serron_backward_from_winners_widened",
+    "serron_derived_supported",
+    "serron_derived_forward",
 )
 
 
@@ -106,6 +109,13 @@ def load() -> ctypes.CDLL:
         lib.serron_backward_from_winners.argtypes = [i32, vp, p64, i64, p64, i64, i32, i64, i32, vp, i32, vp, vp, vp,
                                                      i64, i32, vp]
         lib.serron_backward_from_winners.restype = ctypes.c_int
+        lib.serron_backward_from_winners_widened.argtypes = [i32, vp, i32, p64, i64, p64, i64, i64, i32, vp, i32, vp,
+                                                             i32, vp, vp, i64, i32, vp]
+        lib.serron_backward_from_winners_widened.restype = ctypes.c_int
+        lib.serron_derived_supported.argtypes = [i32, p64, i64, p64, i64]
+        lib.serron_derived_supported.restype = ctypes.c_int
+        lib.serron_derived_forward.argtypes = [i32, vp, p64, i64, vp, p64, i64, i32, i64, vp, vp, vp, i32, i32, vp]
+        lib.serron_derived_forward.restype = ctypes.c_int
         lib.serron_backward_workspace_bytes.argtypes = [p64, i64, p64, i64, i32, i32, i32]
         lib.serron_backward_workspace_bytes.restype = i64
         for name in ("serron_feasible_algos", "serron_heuristic_algo"):

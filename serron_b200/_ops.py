@@ -154,6 +154,46 @@ def forward_autocast(op: int, input_: torch.Tensor, kernel: torch.Tensor, border
     return out, winners, _WINNERS_DIRECT_U8_MAP
 
 
+# derived operations in one launch (serron_derived_forward): the mode codes of the C ABI
+DERIVED_GRADIENT, DERIVED_OPENING, DERIVED_CLOSING, DERIVED_TOP_HAT, DERIVED_BLACK_HAT = range(5)
+
+
+def derived_supported(mode: int, input_: torch.Tensor, kernel: torch.Tensor) -> bool:
+    """The one-launch form of derived operation ``mode`` takes this call (CUDA tensors of one dtype, a
+    4-D input, a 2-D or per-channel 3-D kernel, windows up to 7 a side)."""
+    if not (input_.is_cuda and kernel.is_cuda) or input_.dtype != kernel.dtype or input_.device != kernel.device:
+        return False
+    if input_.dtype not in _lib.DTYPE_CODE or input_.dim() != 4 or input_.numel() == 0:
+        return False
+    if kernel.dim() == 3 and kernel.shape[0] != input_.shape[1] or kernel.dim() not in (2, 3):
+        return False
+    xs, xd = _lib.sizes(input_.shape)
+    ks, kd = _lib.sizes(kernel.shape)
+    return bool(_lib.load().serron_derived_supported(mode, xs, xd, ks, kd))
+
+
+def derived_forward(mode: int, input_: torch.Tensor, kernel: torch.Tensor, border: int
+                    ) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, int]:
+    """Derived operation ``mode`` in one launch: the output and the records (with target maps) of its two
+    primitive operations (gradient: dilation, erosion; others: first, second stage)."""
+    x = input_.contiguous()
+    k = kernel.contiguous()
+    out = torch.empty_like(x)
+    xs, xd = _lib.sizes(x.shape)
+    ks, kd = _lib.sizes(k.shape)
+    lib = _lib.load()
+    nbytes = lib.serron_winners_bytes(xs, xd, _WINNERS_DIRECT_U8_MAP)
+    if nbytes < 0:
+        _lib.raise_for(_lib.ERR_INVALID)
+    win_a = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    win_b = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=x.device)
+    rc = lib.serron_derived_forward(mode, x.data_ptr(), xs, xd, k.data_ptr(), ks, kd, _lib.DTYPE_CODE[x.dtype],
+                                    int(border), out.data_ptr(), win_a.data_ptr(), win_b.data_ptr(),
+                                    _WINNERS_DIRECT_U8_MAP, x.device.index, _lib.stream_of(x))
+    _lib.raise_for(rc)
+    return out, win_a, win_b, _WINNERS_DIRECT_U8_MAP
+
+
 def backward(op: int, grad_output: torch.Tensor, input_: torch.Tensor, kernel: torch.Tensor, border: int,
              flat: bool | None = None, need_kernel_grad: bool = True, algo: int = 0
              ) -> tuple[torch.Tensor, torch.Tensor]:
@@ -201,6 +241,32 @@ def backward_from_winners(op: int, grad_output: torch.Tensor, winners: torch.Ten
                                           int(bool(need_kernel_grad)), winners.data_ptr(), winners_format,
                                           grad_input.data_ptr(), grad_kernel.data_ptr(), workspace.data_ptr(),
                                           ws_bytes, go.device.index, _lib.stream_of(go))
+    _lib.raise_for(rc)
+    return grad_input, grad_kernel
+
+
+def backward_from_winners_widened(op: int, grad_output: torch.Tensor, winners: torch.Tensor, winners_format: int,
+                                  kernel: torch.Tensor, border: int, need_kernel_grad: bool,
+                                  grad_input_dtype: torch.dtype) -> tuple[torch.Tensor, torch.Tensor]:
+    """:func:`backward_from_winners` in float32 arithmetic straight from a float16 / bfloat16 / float32
+    ``grad_output``, with ``grad_input`` rounded to ``grad_input_dtype``: the same values as widening
+    ``grad_output``, gathering in float32 and casting the result (``serron_backward_from_winners_widened``)."""
+    go = grad_output.contiguous()
+    k = kernel.contiguous()
+    grad_input = torch.empty(go.shape, dtype=grad_input_dtype, device=go.device)
+    grad_kernel = torch.empty_like(k)
+    xs, xd = _lib.sizes(go.shape)
+    ks, kd = _lib.sizes(k.shape)
+    lib = _lib.load()
+    ws_bytes = lib.serron_backward_workspace_bytes(xs, xd, ks, kd, int(bool(need_kernel_grad)), winners_format, 1)
+    if ws_bytes < 0:
+        _lib.raise_for(_lib.ERR_INVALID)
+    workspace = torch.empty(max(ws_bytes, 1), dtype=torch.uint8, device=go.device)
+    rc = lib.serron_backward_from_winners_widened(op, go.data_ptr(), _lib.DTYPE_CODE[go.dtype], xs, xd, ks, kd,
+                                                  int(border), int(bool(need_kernel_grad)), winners.data_ptr(),
+                                                  winners_format, grad_input.data_ptr(),
+                                                  _lib.DTYPE_CODE[grad_input_dtype], grad_kernel.data_ptr(),
+                                                  workspace.data_ptr(), ws_bytes, go.device.index, _lib.stream_of(go))
     _lib.raise_for(rc)
     return grad_input, grad_kernel
 

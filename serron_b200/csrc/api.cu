@@ -12,6 +12,7 @@
 #include "direct.cuh"
 #include "recon.cuh"
 #include "recon_persist.cuh"
+#include "derived.cuh"
 #include "recon_scan.cuh"
 #include "segrad.cuh"
 #include "separable.cuh"
@@ -25,6 +26,11 @@ namespace serron {
 template <typename T>
 int sep_fast_fwd_t(int op, int K, bool with_value, bool with_index, const void* x, void* y, void* win, uint32_t* map,
                    long long planes, int H, int W, int border, cudaStream_t stream);
+// the one-launch derived operations (derived.cu)
+bool derived_supported(int mode, long long H, long long W, long long kH, long long kW);
+cudaError_t derived_fwd_launch(int mode, int dtype, const void* x, const void* w, void* y, uint8_t* win_a,
+                               uint8_t* win_b, uint32_t* map_a, uint32_t* map_b, long long planes, int C, int H, int W,
+                               int kH, int kW, int kcs, int border, cudaStream_t stream);
 // the autocast forward (tiled_autocast.cu): float16 values and float32 winners in one pass
 bool autocast_fwd_supported_k(int kH, int kW);
 cudaError_t autocast_fwd_launch(int op, int input_dtype, int K, const void* x, const float* w, __half* y,
@@ -652,6 +658,65 @@ void launch_segrad_t(int op, const Geometry& g, const void* go, const void* win,
     SB_CUDA(cudaGetLastError());
 }
 
+// The pull gather and the structuring-element gradient with float arithmetic, grad_output read as TG and
+// grad_input written as TO (one-byte or two-byte direct records with their target map).
+template <typename TG, typename TO, typename I>
+void launch_backward_widened_t(int op, const Geometry& g, const void* go, const void* win, void* gi, void* gk,
+                               bool need_kg, const uint32_t* map, void* ws, int border, cudaStream_t stream) {
+    const int H = static_cast<int>(g.H), W = static_cast<int>(g.W);
+    const int kH = static_cast<int>(g.kH), kW = static_cast<int>(g.kW);
+    const SumGeom sgeo(kH, kW, sizeof(TG), sizeof(I));
+    const int tiles_x = ceil_div(W, kPullTQ), tiles_y = ceil_div(H, kSumTP);
+    auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    const int go_vec = aligned(go) && (W * sizeof(TG)) % 16 == 0;
+    const int rec_vec = aligned(win) && (W * sizeof(I)) % 16 == 0;
+    const int out_vec = aligned(gi) && (W * sizeof(TO)) % 16 == 0;
+    const int bulk = go_vec && rec_vec;
+    auto run = [&](auto sum) {
+        set_smem(sum, sgeo.smem());
+        SB_CUDA(cudaFuncSetAttribute(sum, cudaFuncAttributePreferredSharedMemoryCarveout, 100));
+        sum<<<grid_1d(g.N * g.C * tiles_x * tiles_y), kSumThreads, sgeo.smem(), stream>>>(
+            static_cast<const TG*>(go), static_cast<const I*>(win), map, static_cast<TO*>(gi), H, W, kH, kW, border,
+            tiles_x, tiles_y, go_vec, rec_vec, out_vec, bulk);
+    };
+    const int box = (sizeof(I) == 1 && kH == kW && (kW & 1) && kW >= 3 && kW <= 15) ? kW : 0;
+    if constexpr (sizeof(I) == 1) {
+        switch (box) {
+        case 3: run(pull_sum_kernel<float, I, 3, TG, TO>); break;
+        case 5: run(pull_sum_kernel<float, I, 5, TG, TO>); break;
+        case 7: run(pull_sum_kernel<float, I, 7, TG, TO>); break;
+        case 9: run(pull_sum_kernel<float, I, 9, TG, TO>); break;
+        case 11: run(pull_sum_kernel<float, I, 11, TG, TO>); break;
+        case 13: run(pull_sum_kernel<float, I, 13, TG, TO>); break;
+        case 15: run(pull_sum_kernel<float, I, 15, TG, TO>); break;
+        default: run(pull_sum_kernel<float, I, 0, TG, TO>); break;
+        }
+    } else {
+        run(pull_sum_kernel<float, I, 0, TG, TO>);
+    }
+    SB_CUDA(cudaGetLastError());
+    if (!need_kg) {
+        SB_CUDA(cudaMemsetAsync(gk, 0, g.kernel_numel() * sizeof(float), stream));
+        return;
+    }
+    const SegradPlan p = segrad_plan(g);
+    const int bins = static_cast<int>(g.kH * g.kW);
+    double* partial = static_cast<double*>(ws);
+    double* gbins = p.global_bins ? reinterpret_cast<double*>(static_cast<char*>(ws) + align256(p.partial_bytes)) : nullptr;
+    const size_t smem = p.global_bins ? 0 : static_cast<size_t>(p.threads) * bins * 8;
+    auto kernel = segrad_partial_kernel<TG, I, false>;
+    set_smem(kernel, smem);
+    kernel<<<dim3(p.chunks, static_cast<unsigned>(g.C)), p.threads, smem, stream>>>(
+        static_cast<const TG*>(go), static_cast<const I*>(win), partial, gbins, static_cast<int>(g.N),
+        static_cast<int>(g.C), H, W, kH, kW, border, p.per_chunk);
+    SB_CUDA(cudaGetLastError());
+    const int out_cells = static_cast<int>(g.kcs ? g.C * bins : bins);
+    segrad_final_kernel<float><<<out_cells, kSegradFinalThreads, 0, stream>>>(
+        partial, static_cast<float*>(gk), static_cast<int>(g.C), p.chunks, bins, g.kcs ? 0 : 1,
+        op == kErode ? -1.0 : 1.0);
+    SB_CUDA(cudaGetLastError());
+}
+
 // `map`: the target map (ready: filled from these records), `ws`: the segrad workspace.
 void launch_backward_from_winners(int op, int dtype, const Geometry& g, const void* go, const void* win, int fmt,
                                   void* gi, void* gk, bool need_kg, uint32_t* map, bool map_ready, void* ws,
@@ -1038,6 +1103,47 @@ int serron_forward_autocast(int32_t op, const void* input, const int64_t* input_
     });
 }
 
+int serron_derived_supported(int32_t mode, const int64_t* input_sizes, int64_t input_dim, const int64_t* kernel_sizes,
+                             int64_t kernel_dim) {
+    if (input_dim != 4 || input_sizes == nullptr || kernel_sizes == nullptr || (kernel_dim != 2 && kernel_dim != 3))
+        return 0;
+    return derived_supported(mode, input_sizes[2], input_sizes[3], kernel_sizes[kernel_dim - 2],
+                             kernel_sizes[kernel_dim - 1])
+               ? 1
+               : 0;
+}
+
+int serron_derived_forward(int32_t mode, const void* input, const int64_t* input_sizes, int64_t input_dim,
+                           const void* kernel, const int64_t* kernel_sizes, int64_t kernel_dim, int32_t dtype,
+                           int64_t border, void* output, void* winners_a, void* winners_b, int32_t winners_format,
+                           int32_t device, void* stream) {
+    return guarded([&] {
+        static const char* const names[] = {"serron.gradient", "serron.opening", "serron.closing", "serron.top_hat",
+                                            "serron.black_hat"};
+        SB_CHECK(mode >= 0 && mode <= 4, "serron: invalid derived operation ", mode);
+        const char* name = names[mode];
+        const Geometry g = parse_geometry(name, input_sizes, input_dim, kernel_sizes, kernel_dim);
+        check_common(name, dtype, border);
+        SB_CHECK(derived_supported(mode, g.H, g.W, g.kH, g.kW), name, ": no one-launch form for a ", g.kH, "x", g.kW,
+                 " window on a ", g.H, "x", g.W, " image (windows up to ", kDerivedMaxK, " a side)");
+        const int fmt = SERRON_WINNERS_DIRECT_U8 | SERRON_WINNERS_MAP;
+        SB_CHECK(winners_format == fmt, name, ": winner format ", winners_format, " (", fmt, " expected)");
+        DeviceScope scope(device);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (g.numel() == 0) return;
+        SB_CHECK(input && kernel && output && winners_a && winners_b, name, ": null tensor pointer");
+        const int64_t map_bytes = pull_map_words(g.N * g.C, g.H, g.W) * 4;
+        uint32_t* map_a = reinterpret_cast<uint32_t*>(static_cast<char*>(winners_a) + records_bytes(g, fmt));
+        uint32_t* map_b = reinterpret_cast<uint32_t*>(static_cast<char*>(winners_b) + records_bytes(g, fmt));
+        SB_CUDA(cudaMemsetAsync(map_a, 0, map_bytes, s));
+        SB_CUDA(cudaMemsetAsync(map_b, 0, map_bytes, s));
+        SB_CUDA(derived_fwd_launch(mode, dtype, input, kernel, output, static_cast<uint8_t*>(winners_a),
+                                   static_cast<uint8_t*>(winners_b), map_a, map_b, g.N * g.C, static_cast<int>(g.C),
+                                   static_cast<int>(g.H), static_cast<int>(g.W), static_cast<int>(g.kH),
+                                   static_cast<int>(g.kW), static_cast<int>(g.kcs), static_cast<int>(border), s));
+    });
+}
+
 int64_t serron_winners_bytes(const int64_t* sizes, int64_t dim, int32_t winners_format) {
     int64_t out = -1;
     const int rc = guarded([&] {
@@ -1140,6 +1246,67 @@ int serron_backward_from_winners(int32_t op, const void* grad_output, const int6
         launch_backward_from_winners(op, dtype, g, grad_output, winners, winners_format, grad_input, grad_kernel,
                                      need_kernel_grad != 0, map, has_map, has_map ? ws : ws + map_workspace(g),
                                      static_cast<int>(border), info.smem_optin, s);
+    });
+}
+
+int serron_backward_from_winners_widened(int32_t op, const void* grad_output, int32_t grad_output_dtype,
+                                         const int64_t* sizes, int64_t dim, const int64_t* kernel_sizes,
+                                         int64_t kernel_dim, int64_t border, int32_t need_kernel_grad,
+                                         const void* winners, int32_t winners_format, void* grad_input,
+                                         int32_t grad_input_dtype, void* grad_kernel, void* workspace,
+                                         int64_t workspace_bytes, int32_t device, void* stream) {
+    return guarded([&] {
+        const char* name = bwd_name(op);
+        SB_CHECK(op == kErode || op == kDilate, "serron: invalid op ", op);
+        const Geometry g = parse_geometry(name, sizes, dim, kernel_sizes, kernel_dim);
+        check_common(name, kF32, border);
+        auto half_or_float = [](int32_t d) { return d == kF32 || d == kF16 || d == kBF16; };
+        SB_CHECK(half_or_float(grad_output_dtype) && half_or_float(grad_input_dtype), name,
+                 ": the widened backward reads and writes float32, float16 or bfloat16");
+        const int base = base_format(winners_format);
+        SB_CHECK((base == SERRON_WINNERS_DIRECT_U8 || base == SERRON_WINNERS_DIRECT_U16) &&
+                     format_has_map(winners_format) && (winners_format & ~(SERRON_WINNERS_MAP | 0xf)) == 0 &&
+                     base == direct_format(g.kH, g.kW),
+                 name, ": the widened backward needs direct one- or two-byte records with their target map, got format ",
+                 winners_format);
+        DeviceScope scope(device);
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        if (g.numel() == 0) {
+            if (g.kernel_numel() > 0) SB_CUDA(cudaMemsetAsync(grad_kernel, 0, g.kernel_numel() * sizeof(float), s));
+            return;
+        }
+        const int64_t need = backward_workspace(g, need_kernel_grad != 0, winners_format, true);
+        if (workspace_bytes < need)
+            throw Failure{SERRON_ERR_WORKSPACE, concat(name, ": workspace of ", workspace_bytes, " bytes, ", need, " needed")};
+        SB_CHECK(grad_output && winners && grad_input && grad_kernel, name, ": null tensor pointer");
+        const DeviceInfo info = device_info(device);
+        SB_CHECK(pull_applicable(g, static_cast<int>(border), elem_size(grad_output_dtype), format_bytes(winners_format),
+                                 info.smem_optin),
+                 name, ": the widened backward does not fit this window and image");
+        const uint32_t* map = reinterpret_cast<const uint32_t*>(static_cast<const char*>(winners) +
+                                                                records_bytes(g, winners_format));
+        auto with_index = [&](auto tg, auto to) {
+            using TG = decltype(tg);
+            using TO = decltype(to);
+            if (base == SERRON_WINNERS_DIRECT_U8)
+                launch_backward_widened_t<TG, TO, uint8_t>(op, g, grad_output, winners, grad_input, grad_kernel,
+                                                           need_kernel_grad != 0, map, workspace, static_cast<int>(border), s);
+            else
+                launch_backward_widened_t<TG, TO, uint16_t>(op, g, grad_output, winners, grad_input, grad_kernel,
+                                                            need_kernel_grad != 0, map, workspace, static_cast<int>(border), s);
+        };
+        auto with_out = [&](auto tg) {
+            switch (grad_input_dtype) {
+            case kF32: with_index(tg, float{}); break;
+            case kF16: with_index(tg, __half{}); break;
+            default: with_index(tg, __nv_bfloat16{}); break;
+            }
+        };
+        switch (grad_output_dtype) {
+        case kF32: with_out(float{}); break;
+        case kF16: with_out(__half{}); break;
+        default: with_out(__nv_bfloat16{}); break;
+        }
     });
 }
 

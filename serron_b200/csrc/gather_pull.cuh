@@ -278,8 +278,8 @@ struct SumGeom {
 //   rec      tap row of box row 0 at box column 0 (a byte address; rows rq bytes apart, rq % 4 == 0)
 //   gp       grad_output of box row 0 at box column 0 (rows gq elements apart)
 //   rows_ok  bit r: box row r lies in the image;  keep[g]: 0x80 in byte k where box column 4g+k does
-template <int KB, typename T>
-__device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed(const uint8_t* rec, int rq, const T* gp, int gq,
+template <int KB, typename T, typename TG>
+__device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed(const uint8_t* rec, int rq, const TG* gp, int gq,
                                                                     uint32_t rows_ok,
                                                                     const uint32_t (&keep)[(KB + 3) / 4]) {
     using G = typename GradAcc<T>::type;
@@ -307,7 +307,7 @@ __device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed(const uint8_
         G v[KB];
 #pragma unroll
         for (int j = 0; j < KB; ++j)
-            v[j] = (m[j >> 2] >> (8 * (j & 3) + 7)) & 1u ? static_cast<G>(Storage<T>::load(gp[j])) : G(0);
+            v[j] = (m[j >> 2] >> (8 * (j & 3) + 7)) & 1u ? static_cast<G>(Storage<TG>::load(gp[j])) : G(0);
 #pragma unroll
         for (int j = 0; j < KB; ++j)
             if ((m[j >> 2] >> (8 * (j & 3) + 7)) & 1u) acc = GradAcc<T>::add(acc, v[j]);
@@ -315,8 +315,8 @@ __device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed(const uint8_
     return acc;
 }
 
-template <int KB, typename T>
-__device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed_clip(const uint8_t* rec, int rq, const T* gp,
+template <int KB, typename T, typename TG>
+__device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed_clip(const uint8_t* rec, int rq, const TG* gp,
                                                                          int gq, int x, int y, int H, int W) {
     constexpr int a = KB / 2, NG = (KB + 3) / 4;
     const int rlo = max(0, a - x), rhi = min(KB - 1, H - 1 - x + a);
@@ -333,28 +333,32 @@ __device__ __forceinline__ typename GradAcc<T>::type pull_box_fixed_clip(const u
         }
         keep[g] = k;
     }
-    return pull_box_fixed<KB, T>(rec, rq, gp, gq, rows_ok, keep);
+    return pull_box_fixed<KB, T, TG>(rec, rq, gp, gq, rows_ok, keep);
 }
 
 // KB > 0: the box of a KB x KB window with one-byte records, unrolled (one kernel per size keeps each
 // one's code small); KB == 0: any window, walked generically.  With `bulk`, grad_output and the records
 // of each staged row arrive by one bulk copy each (rows 16-byte aligned: the host checks pointers and W).
-template <typename T, typename I, int KB>
-__global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restrict__ go, const I* __restrict__ win,
+// T is the arithmetic (the sums run as the reference adds in T); grad_output is read as TG and grad_input
+// written as TO, by default T: with TG = float16 / bfloat16 and T = float, grad_output is widened on load
+// (exactly) and each sum rounded to TO once at its store, which equals casting grad_output to float,
+// gathering in float and casting the result.
+template <typename T, typename I, int KB, typename TG = T, typename TO = T>
+__global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const TG* __restrict__ go, const I* __restrict__ win,
                                                                const uint32_t* __restrict__ map,
-                                                               T* __restrict__ gi, int H, int W, int kH, int kW,
+                                                               TO* __restrict__ gi, int H, int W, int kH, int kW,
                                                                int border, int tiles_x, int tiles_y, int go_vec,
                                                                int rec_vec, int out_vec, int bulk) {
     static_assert(KB == 0 || sizeof(I) == 1, "the unrolled box reads one-byte records");
     using G = typename GradAcc<T>::type;
     constexpr int TP = kSumTP, TQ = kPullTQ, NT = kSumThreads, NWORDS = TP * TQ / 32;
     constexpr uint32_t kNone = IndexTraits<I>::none;
-    const SumGeom geo(kH, kW, sizeof(T), sizeof(I));
+    const SumGeom geo(kH, kW, sizeof(TG), sizeof(I));
     const int aH = geo.aH, aW = geo.aW, hq = geo.hq, gv = geo.gv, goff = geo.goff, gq = geo.gq;
     const int rv = geo.rv, roff = geo.roff, rq = geo.rq;
     const int S = 2 * aW + 1;
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    T* goS = reinterpret_cast<T*>(smem_raw);                                          // [hr][gq]
+    TG* goS = reinterpret_cast<TG*>(smem_raw);                                        // [hr][gq]
     I* recS = reinterpret_cast<I*>(smem_raw + geo.go_b);                              // [hr][rq]
     uint16_t* listS = reinterpret_cast<uint16_t*>(smem_raw + geo.go_b + geo.rec_b);   // [TP * TQ]
     int* countS = reinterpret_cast<int*>(smem_raw + geo.go_b + geo.rec_b + geo.list_b);
@@ -377,25 +381,25 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
     }
     // the tile is zeroed first, in 16-byte stores; the winners' sums are stored over the zeros after the
     // barriers below (ordered within the CTA)
-    T* gip = gi + plane * H * W;
+    TO* gip = gi + plane * H * W;
     {
-        constexpr int OV = 16 / int(sizeof(T));
+        constexpr int OV = 16 / int(sizeof(TO));
         for (int i = tid; i < TP * TQ / OV; i += NT) {
             const int pr = i / (TQ / OV), pc = (i - pr * (TQ / OV)) * OV;
             const int r = r0 + pr, c = c0 + pc;
             if (r >= H || c >= W) continue;
-            T* dst = gip + static_cast<long long>(r) * W + c;
+            TO* dst = gip + static_cast<long long>(r) * W + c;
             if (out_vec && c + OV <= W) {
                 *reinterpret_cast<uint4*>(dst) = make_uint4(0, 0, 0, 0);
             } else {
-                for (int e = 0; e < OV && c + e < W; ++e) dst[e] = Storage<T>::store(0.0f);
+                for (int e = 0; e < OV && c + e < W; ++e) dst[e] = Storage<TO>::store(0.0f);
             }
         }
     }
     if (!__syncthreads_or(bits != 0u)) return;  // no winner in the tile
 
     // stage grad_output and records of output rows [r0 - aH, r0 + TP + aH) inside the image
-    const T* gop = go + plane * H * W;
+    const TG* gop = go + plane * H * W;
     const I* wp = win + plane * H * W;
     const int lo = max(0, r0 - aH), hi = min(H, r0 + TP + aH);
     __shared__ __align__(8) uint64_t bar;
@@ -404,7 +408,7 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
         const int gcol0 = c0 - aW - goff, rcol0 = c0 - aW - roff;  // 16-byte aligned in the image row
         const int gc_lo = max(gcol0, 0), gc_hi = min(gcol0 + gq, W);
         const int rc_lo = max(rcol0, 0), rc_hi = min(rcol0 + rq, W);
-        const unsigned gbytes = static_cast<unsigned>(gc_hi - gc_lo) * sizeof(T);
+        const unsigned gbytes = static_cast<unsigned>(gc_hi - gc_lo) * sizeof(TG);
         const unsigned rbytes = static_cast<unsigned>(rc_hi - rc_lo) * sizeof(I);
         if (tid == 0) {
             mbar_init(&bar, 1);
@@ -423,7 +427,7 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
             for (int i = tid; i < (hi - lo) * gpad; i += NT) {
                 const int sr = lo + i / gpad - (r0 - aH), q = i % gpad;
                 const int col = q < gc_lo - gcol0 ? q : gc_hi - gcol0 + (q - (gc_lo - gcol0));
-                goS[sr * gq + col] = Storage<T>::store(0.0f);
+                goS[sr * gq + col] = Storage<TG>::store(0.0f);
             }
             for (int i = tid; i < (hi - lo) * rpad; i += NT) {
                 const int sr = lo + i / rpad - (r0 - aH), q = i % rpad;
@@ -438,12 +442,12 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
         for (int i = tid; i < (hi - lo) * nchg; i += NT) {
             const int r = static_cast<int>(__umulhi(static_cast<uint32_t>(i), mg)), k = i - r * nchg;
             const int h = lo + r, col = c0 - aW - goff + k * gv;
-            T* dst = goS + (h - (r0 - aH)) * gq + k * gv;
-            const T* src = gop + static_cast<long long>(h) * W + col;
+            TG* dst = goS + (h - (r0 - aH)) * gq + k * gv;
+            const TG* src = gop + static_cast<long long>(h) * W + col;
             if (go_vec && col >= 0 && col + gv <= W) {
                 pg_cp_async16(dst, src);
             } else {
-                for (int e = 0; e < gv; ++e) dst[e] = (col + e >= 0 && col + e < W) ? src[e] : Storage<T>::store(0.0f);
+                for (int e = 0; e < gv; ++e) dst[e] = (col + e >= 0 && col + e < W) ? src[e] : Storage<TG>::store(0.0f);
             }
         }
         for (int i = tid; i < (hi - lo) * nchr; i += NT) {
@@ -483,7 +487,7 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
         if (!__syncthreads_and(mbar_wait(&bar, 0))) {
             for (int i = tid; i < TP * TQ; i += NT) {
                 const int r = r0 + i / TQ, c = c0 + i % TQ;
-                if (r < H && c < W) gip[static_cast<long long>(r) * W + c] = Storage<T>::store(__int_as_float(0x7fffffff));
+                if (r < H && c < W) gip[static_cast<long long>(r) * W + c] = Storage<TO>::store(__int_as_float(0x7fffffff));
             }
             return;
         }
@@ -544,21 +548,21 @@ __global__ void __launch_bounds__(kSumThreads) pull_sum_kernel(const T* __restri
         G acc = G(0);
         if constexpr (KB > 0) {
             const uint8_t* rec = reinterpret_cast<const uint8_t*>(recS) + pr * rq + roff + pc;
-            const T* gp = goS + pr * gq + goff + pc;
-            acc = pull_box_fixed_clip<KB, T>(rec, rq, gp, gq, x, y, H, W);
+            const TG* gp = goS + pr * gq + goff + pc;
+            acc = pull_box_fixed_clip<KB, T, TG>(rec, rq, gp, gq, x, y, H, W);
         } else {
             for (int h = max(0, x - aH); h <= min(H - 1, x + aH); ++h) {
                 const int lh = h - (r0 - aH);
                 const int jlo = max(0, aW - y), jhi = min(2 * aW, W - 1 - y + aW);
                 const I* trow = recS + lh * rq + roff + pc;  // box column j at trow[j]
-                const T* grow = goS + lh * gq + goff + pc;
+                const TG* grow = goS + lh * gq + goff + pc;
                 const int e0 = (x - h + aH) * S + 2 * aW;     // tap selecting (x, y) from box column 0
                 for (int j = jlo; j <= jhi; ++j)
                     if (static_cast<int>(trow[j]) == e0 - j)
-                        acc = GradAcc<T>::add(acc, static_cast<G>(Storage<T>::load(grow[j])));
+                        acc = GradAcc<T>::add(acc, static_cast<G>(Storage<TG>::load(grow[j])));
             }
         }
-        gip[static_cast<long long>(x) * W + y] = Storage<T>::store(static_cast<typename Storage<T>::acc>(acc));
+        gip[static_cast<long long>(x) * W + y] = Storage<TO>::store(static_cast<typename Storage<TO>::acc>(acc));
     }
 }
 

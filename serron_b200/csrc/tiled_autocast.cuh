@@ -14,8 +14,9 @@
 //            two halves rounds to half exactly as the half difference does (24 >= 2 * 11 + 2 bits), so the
 //            results agree bit for bit.  NaN taps never win (the half2 min/max returns the other value);
 //            the neutral element stays when nothing else is there.
-//   winner   the first strict improvement in (di, dj) order of float(x) -/+ w in float32, ties with the
-//            running best tracked and such windows settled in double, as the reference CPU compares.
+//   winner   the first strict improvement in (di, dj) order of float(x) -/+ w in float32; a thread notes
+//            whether any tap of its outputs compared equal to a running best, and then settles its
+//            outputs' windows in double, as the reference CPU compares (exact weights need neither).
 //
 // A CTA computes a 32 x 64 output tile, eight adjacent outputs per thread (lane = tile row, warp = group
 // of eight columns).  The tile's input rows (plus the window's halo) arrive by one bulk copy each (the
@@ -78,7 +79,7 @@ __device__ __forceinline__ __half2 ac_best2(__half2 a, __half2 b) {
 // TI: input storage (float, __half, __nv_bfloat16); weights are float32, per channel (kcs = K * K) or
 // shared (kcs = 0).  `bulk`: rows of x start on 16-byte boundaries (pointer and W checked by the host).
 template <typename TI, int OP, int K>
-__global__ void __launch_bounds__(kAcThreads, 2) tiled_autocast_fwd_kernel(
+__global__ void __launch_bounds__(kAcThreads, 3) tiled_autocast_fwd_kernel(
     const TI* __restrict__ x, const float* __restrict__ w, __half* __restrict__ y, uint8_t* __restrict__ win,
     uint32_t* __restrict__ map, int C, int H, int W, int kcs, int border, int tiles_x, int tiles_y, int bulk,
     int out_vec) {
@@ -164,7 +165,7 @@ __global__ void __launch_bounds__(kAcThreads, 2) tiled_autocast_fwd_kernel(
     __half2 acc[kAcQ / 2];
     float best[kAcQ];
     int tap[kAcQ];
-    unsigned tie = 0;
+    bool tie = false;  // some tap of some output compared equal to that output's running best
     {
         const __half hn = __float2half_rn(neutral);
 #pragma unroll
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(kAcThreads, 2) tiled_autocast_fwd_kernel(
 #pragma unroll
             for (int k = 0; k < kAcQ; ++k) {
                 const float v = Op<OP>::tap(s[k + dj], wv);
-                if (!exact) tie |= (v == best[k] ? 1u : 0u) << k;
+                if (!exact) tie |= v == best[k];
                 if (Op<OP>::better(v, best[k])) {
                     best[k] = v;
                     tap[k] = t_idx;
@@ -234,8 +235,9 @@ __global__ void __launch_bounds__(kAcThreads, 2) tiled_autocast_fwd_kernel(
 #pragma unroll
         for (int k = 0; k < kAcQ; ++k) {
             vals[k] = (k & 1) ? __high2half(acc[k >> 1]) : __low2half(acc[k >> 1]);
-            if (((tie >> k) & 1u) && best[k] != neutral) {
-                // a float tie with the running best: settle it the way the reference CPU does, in double
+            if (tie && best[k] != neutral) {
+                // a float tie with a running best in this thread: settle its outputs the way the reference
+                // CPU does, in double (rare: it takes two taps whose float32 results coincide)
                 auto sample = [&](int di_, int dj_, float& s_) {
                     s_ = xs[(lr + di_) * XP + q0 + k + dj_];
                     return true;

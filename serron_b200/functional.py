@@ -1,8 +1,11 @@
 """Stateless morphology on CUDA tensors.
 
 Same functions, signatures, defaults and errors as packages/serron/torch-ext/serron/functional.py.
-``erosion`` / ``dilation`` go through the autograd functions; the derived operations are the same
-compositions; the reconstructions run on the library's fixed-point solver instead of a Python loop.
+``erosion`` / ``dilation`` go through the autograd functions.  The derived operations run in one launch
+(``serron_derived_forward``: both extremes from one staged tile for the gradient, the intermediate image
+in shared memory for the others) when the input and the structuring element share a dtype, autocast is
+off and the window is at most 7 a side; otherwise they are the reference's compositions.  Both give the
+same bits.  The reconstructions run on the library's fixed-point solver instead of a Python loop.
 """
 
 from __future__ import annotations
@@ -11,7 +14,7 @@ import torch
 
 from . import _flatness, _ops
 from ._autotune import ensure_loaded
-from .autograd import _DilateFunction, _ErodeFunction
+from .autograd import _DerivedFunction, _DilateFunction, _ErodeFunction
 from .enums import BORDER_TO_INT, BorderMode
 
 
@@ -25,28 +28,44 @@ def dilation(input_: torch.Tensor, kernel: torch.Tensor, *, border: BorderMode =
     return _DilateFunction.apply(input_, kernel, BORDER_TO_INT[border])
 
 
+def _fused(mode: int, input_: torch.Tensor, kernel: torch.Tensor) -> bool:
+    """Whether derived operation ``mode`` runs in one launch for these arguments (same bits either way)."""
+    return (isinstance(input_, torch.Tensor) and isinstance(kernel, torch.Tensor) and input_.is_cuda
+            and not torch.is_autocast_enabled("cuda") and _ops.derived_supported(mode, input_, kernel))
+
+
 def opening(input_: torch.Tensor, kernel: torch.Tensor, *, border: BorderMode = BorderMode.REPLICATE) -> torch.Tensor:
     """Erosion followed by dilation."""
+    if _fused(_ops.DERIVED_OPENING, input_, kernel):
+        return _DerivedFunction.apply(input_, kernel, BORDER_TO_INT[border], _ops.DERIVED_OPENING)
     return dilation(erosion(input_, kernel, border=border), kernel, border=border)
 
 
 def closing(input_: torch.Tensor, kernel: torch.Tensor, *, border: BorderMode = BorderMode.REPLICATE) -> torch.Tensor:
     """Dilation followed by erosion."""
+    if _fused(_ops.DERIVED_CLOSING, input_, kernel):
+        return _DerivedFunction.apply(input_, kernel, BORDER_TO_INT[border], _ops.DERIVED_CLOSING)
     return erosion(dilation(input_, kernel, border=border), kernel, border=border)
 
 
 def gradient(input_: torch.Tensor, kernel: torch.Tensor, *, border: BorderMode = BorderMode.REPLICATE) -> torch.Tensor:
     """Morphological gradient ``dilation(input) - erosion(input)``."""
+    if _fused(_ops.DERIVED_GRADIENT, input_, kernel):
+        return _DerivedFunction.apply(input_, kernel, BORDER_TO_INT[border], _ops.DERIVED_GRADIENT)
     return dilation(input_, kernel, border=border) - erosion(input_, kernel, border=border)
 
 
 def top_hat(input_: torch.Tensor, kernel: torch.Tensor, *, border: BorderMode = BorderMode.REPLICATE) -> torch.Tensor:
     """White top-hat ``input - opening(input)``."""
+    if _fused(_ops.DERIVED_TOP_HAT, input_, kernel):
+        return _DerivedFunction.apply(input_, kernel, BORDER_TO_INT[border], _ops.DERIVED_TOP_HAT)
     return input_ - opening(input_, kernel, border=border)
 
 
 def black_hat(input_: torch.Tensor, kernel: torch.Tensor, *, border: BorderMode = BorderMode.REPLICATE) -> torch.Tensor:
     """Black top-hat ``closing(input) - input``."""
+    if _fused(_ops.DERIVED_BLACK_HAT, input_, kernel):
+        return _DerivedFunction.apply(input_, kernel, BORDER_TO_INT[border], _ops.DERIVED_BLACK_HAT)
     return closing(input_, kernel, border=border) - input_
 
 
