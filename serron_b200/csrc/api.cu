@@ -530,9 +530,16 @@ SegradPlan segrad_plan(const Geometry& g) {
     const int64_t max_chunks = std::max<int64_t>(1, total_chunks / std::max<int64_t>(g.C, 1));
     p.chunks = static_cast<int>(std::clamp<int64_t>((per_channel + 16383) / 16384, 1, max_chunks));
     p.per_chunk = (per_channel + p.chunks - 1) / p.chunks;
+    p.per_chunk = (p.per_chunk + 15) / 16 * 16;  // whole 16-output groups for the vector path
     p.partial_bytes = g.C * p.chunks * bins * 8;
     p.bins_bytes = p.global_bins ? g.C * p.chunks * int64_t(p.threads) * bins * 8 : 0;
     return p;
+}
+// The SE-gradient kernel's 16-output vector path: direct records, whole 16-output groups per plane,
+// 16-byte aligned go and records.
+int segrad_vec_ok(const Geometry& g, const void* go, const void* win, bool sep) {
+    auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+    return !sep && (g.H * g.W) % 16 == 0 && aligned(go) && aligned(win) ? 1 : 0;
 }
 int64_t segrad_workspace(const Geometry& g, bool need_kg) {
     if (!need_kg) return 0;
@@ -645,10 +652,11 @@ void launch_segrad_t(int op, const Geometry& g, const void* go, const void* win,
     const size_t smem = p.global_bins ? 0 : static_cast<size_t>(p.threads) * bins * 8;
     auto kernel = segrad_partial_kernel<T, I, SEP>;
     set_smem(kernel, smem);
+    const int vec = segrad_vec_ok(g, go, win, SEP);
     kernel<<<dim3(p.chunks, static_cast<unsigned>(g.C)), p.threads, smem, stream>>>(
         static_cast<const T*>(go), static_cast<const I*>(win), partial, gbins, static_cast<int>(g.N),
         static_cast<int>(g.C), static_cast<int>(g.H), static_cast<int>(g.W), static_cast<int>(g.kH),
-        static_cast<int>(g.kW), border, p.per_chunk);
+        static_cast<int>(g.kW), border, p.per_chunk, vec);
     SB_CUDA(cudaGetLastError());
     const int out_cells = static_cast<int>(g.kcs ? g.C * bins : bins);
     const double sign = op == kErode ? -1.0 : 1.0;
@@ -708,7 +716,7 @@ void launch_backward_widened_t(int op, const Geometry& g, const void* go, const 
     set_smem(kernel, smem);
     kernel<<<dim3(p.chunks, static_cast<unsigned>(g.C)), p.threads, smem, stream>>>(
         static_cast<const TG*>(go), static_cast<const I*>(win), partial, gbins, static_cast<int>(g.N),
-        static_cast<int>(g.C), H, W, kH, kW, border, p.per_chunk);
+        static_cast<int>(g.C), H, W, kH, kW, border, p.per_chunk, segrad_vec_ok(g, go, win, false));
     SB_CUDA(cudaGetLastError());
     const int out_cells = static_cast<int>(g.kcs ? g.C * bins : bins);
     segrad_final_kernel<float><<<out_cells, kSegradFinalThreads, 0, stream>>>(

@@ -381,7 +381,10 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
     }
     __syncthreads();
 
-    const int lr = tid >> 3, c0 = (tid & 7) * Q;  // output row, first of eight columns
+    // output row and first of eight columns: a warp takes 8 rows x 4 column groups, so with the odd pitch
+    // its 32 loads of a sample position hit 32 distinct banks
+    const int lane = tid & 31, wq = tid >> 5;
+    const int lr = 8 * (wq & 3) + (lane & 7), c0 = (4 * (wq >> 2) + (lane >> 3)) * Q;
     const int oh = oh0 + lr;
     const bool active = !(oh >= H || ow0 + c0 >= W);
     if (active) {

@@ -8,6 +8,8 @@
 
 #include "common.cuh"
 
+#include <cstring>
+
 namespace serron {
 
 // Winner tap (di*kW + dj) of output `o` at (oh, ow) of plane `plane_base`, or -1.
@@ -26,10 +28,14 @@ __device__ __forceinline__ int winner_tap(const I* __restrict__ win, long long p
 
 // grid = (chunks, C).  Bins live in shared memory when `bins_global` is null, else in
 // bins_global[(blockIdx.y * gridDim.x + blockIdx.x) * blockDim.x + tid][bins].
+//
+// With `vec` (direct records, H * W and the chunk length multiples of 16, go and win 16-byte aligned) a
+// thread takes 16 consecutive outputs at a time in 16-byte loads, two groups in flight: the kernel streams
+// at memory speed instead of waiting on one-byte loads.
 template <typename T, typename I, bool SEP>
 __global__ void segrad_partial_kernel(const T* __restrict__ go, const I* __restrict__ win,
                                       double* __restrict__ partial, double* __restrict__ bins_global, int N, int C,
-                                      int H, int W, int kH, int kW, int border, long long per_chunk) {
+                                      int H, int W, int kH, int kW, int border, long long per_chunk, int vec) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     const int bins = kH * kW;
     const int nthr = blockDim.x, tid = threadIdx.x;
@@ -43,7 +49,42 @@ __global__ void segrad_partial_kernel(const T* __restrict__ go, const I* __restr
     const long long start = blockIdx.x * per_chunk;
     const long long end = min(start + per_chunk, total);
     long long e = start + tid;
-    if (e < end) {
+    if (!SEP && vec) {
+        constexpr int V = 16, RW = V * int(sizeof(I)) / 16, GW = V * int(sizeof(T)) / 16;  // uint4 words per group
+        auto load_group = [&](long long q, uint4 (&r)[RW], uint4 (&g)[GW]) {
+            const long long e16 = q * V, n = e16 / hw, off = (n * C + c) * hw + (e16 - n * hw);
+            const uint4* rp = reinterpret_cast<const uint4*>(win + off);
+            const uint4* gp = reinterpret_cast<const uint4*>(go + off);
+#pragma unroll
+            for (int i = 0; i < RW; ++i) r[i] = __ldg(rp + i);
+#pragma unroll
+            for (int i = 0; i < GW; ++i) g[i] = __ldg(gp + i);
+        };
+        auto add_group = [&](const uint4 (&r)[RW], const uint4 (&g)[GW]) {
+            I rec[V];
+            T val[V];
+            memcpy(rec, r, sizeof(rec));
+            memcpy(val, g, sizeof(val));
+#pragma unroll
+            for (int i = 0; i < V; ++i)
+                if (static_cast<uint32_t>(rec[i]) != IndexTraits<I>::none)
+                    mine[rec[i]] += static_cast<double>(Storage<T>::load(val[i]));
+        };
+        const long long q1 = end / V;
+        long long q = start / V + tid;
+        for (; q + nthr < q1; q += 2 * static_cast<long long>(nthr)) {
+            uint4 ra[RW], ga[GW], rb[RW], gb[GW];
+            load_group(q, ra, ga);
+            load_group(q + nthr, rb, gb);
+            add_group(ra, ga);
+            add_group(rb, gb);
+        }
+        if (q < q1) {
+            uint4 ra[RW], ga[GW];
+            load_group(q, ra, ga);
+            add_group(ra, ga);
+        }
+    } else if (e < end) {
         // one division per thread; the position then advances by the block size.  Four outputs are
         // read before any is accumulated, so each thread keeps several loads in flight.
         long long n = e / hw;
