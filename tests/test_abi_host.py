@@ -192,3 +192,43 @@ def test_reconstruction_validation():
     bad[1, 1] = -1.0
     with pytest.raises(ValueError, match="anchor tap"):
         serron_b200.reconstruction_by_dilation(mask, mask, bad)
+
+
+def _sizes(shape):
+    return (ctypes.c_int64 * len(shape))(*shape), len(shape)
+
+
+def test_derived_supported_bounds(lib):
+    """The one-launch derived operations take windows up to 7 a side, and (modes 1-4) images at least as
+    large as the window; host only."""
+    cases = [
+        (0, (1, 1, 40, 40), (7, 7), 1), (0, (1, 1, 40, 40), (8, 3), 0), (0, (1, 1, 3, 3), (7, 7), 1),
+        (1, (1, 1, 40, 40), (7, 7), 1), (1, (1, 1, 6, 40), (7, 7), 0), (3, (2, 3, 7, 7), (3, 7, 7), 1),
+        (4, (1, 1, 40, 40), (1, 7), 1), (5, (1, 1, 40, 40), (3, 3), 0), (2, (1, 1, 40), (3, 3), 0),
+    ]
+    for mode, xshape, kshape, want in cases:
+        xs, xd = _sizes(xshape)
+        ks, kd = _sizes(kshape)
+        assert lib.serron_derived_supported(mode, xs, xd, ks, kd) == want, (mode, xshape, kshape)
+
+
+def test_new_entry_points_validate_before_device_work(lib):
+    from serron_b200 import _lib
+
+    xs, xd = _sizes((1, 1, 40, 40))
+    ks, kd = _sizes((9, 9))
+    rc = lib.serron_derived_forward(1, None, xs, xd, None, ks, kd, 0, 1, None, None, None, 0x11, 0, None)
+    assert rc == _lib.ERR_INVALID and b"no one-launch form" in lib.serron_last_error()
+    ks3, kd3 = _sizes((3, 3))
+    rc = lib.serron_derived_forward(1, None, xs, xd, None, ks3, kd3, 0, 1, None, None, None, 0x12, 0, None)
+    assert rc == _lib.ERR_INVALID and b"winner format" in lib.serron_last_error()
+    rc = lib.serron_backward_from_winners_widened(0, None, 1, xs, xd, ks3, kd3, 1, 0, None, 0x11, None, 2, None,
+                                                  None, 0, 0, None)
+    assert rc == _lib.ERR_INVALID and b"float32, float16 or bfloat16" in lib.serron_last_error()
+    rc = lib.serron_backward_from_winners_widened(0, None, 2, xs, xd, ks3, kd3, 1, 0, None, 0x4, None, 3, None,
+                                                  None, 0, 0, None)
+    assert rc == _lib.ERR_INVALID and b"direct one- or two-byte records" in lib.serron_last_error()
+    steps = ctypes.c_int64(0)
+    rc = lib.serron_reconstruct_from_edges(1, None, None, xs, xd, None, ks3, kd3, 0, 2, -1, 0, None, None, 0, 0, None,
+                                           ctypes.byref(steps))
+    assert rc == _lib.ERR_INVALID and b"seed_top and seed_bottom" in lib.serron_last_error()
