@@ -72,6 +72,8 @@ struct Op<kErode> {
     // strict "a is better than b"; false whenever either is NaN
     template <typename A>
     static __device__ __forceinline__ bool better(A a, A b) { return a < b; }
+    template <typename A>
+    static __device__ __forceinline__ bool better_eq(A a, A b) { return a <= b; }
     static constexpr float se_sign = -1.0f;
 };
 template <>
@@ -82,6 +84,8 @@ struct Op<kDilate> {
     static __device__ __forceinline__ A tap(A s, A w) { return s + w; }
     template <typename A>
     static __device__ __forceinline__ bool better(A a, A b) { return a > b; }
+    template <typename A>
+    static __device__ __forceinline__ bool better_eq(A a, A b) { return a >= b; }
     static constexpr float se_sign = 1.0f;
 };
 

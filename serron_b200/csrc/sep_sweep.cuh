@@ -11,8 +11,10 @@
 //   column pass  the same over the row results.
 // With a winner buffer every output gets the direct tap di * K + dj of its winner (di from the column
 // pass, dj from the row pass of the winning row), the record the direct kernels write.
-// Compare-selects keep the first extremum (the reference's tie rule); NaN samples enter as the
-// neutral element, so they never win.
+// Compare-selects keep the first extremum (the reference's tie rule).  A NaN sample never wins: a sample
+// is taken only when it compares at least as good (suffix scan, towards lower offsets) or strictly better
+// (prefix scan) than the running best, which starts at the neutral element, and a compare with a NaN is
+// false.  Three CTAs per SM (80 registers: no spills).
 #pragma once
 
 #include "common.cuh"
@@ -57,44 +59,35 @@ struct SweepGeom {
 };
 
 // One run of K windows [m, m+K-1], m = 0..K-1, over samples v[0..2K-2]: value and first-extremum
-// offset (window-relative) of each.  Ties keep the lower offset.
+// offset (window-relative) of each.  Ties keep the lower offset; a window of NaNs only yields the neutral
+// element (its offset is then meaningless: such outputs get the "none" record).
 template <int K, int OP, bool IDX, typename Emit>
 __device__ __forceinline__ void sweep_run(const float (&v)[2 * K - 1], Emit emit) {
+    const float neutral = Op<OP>::template neutral<float>();
     float sv[K];
     int si[K];
-    sv[K - 1] = v[K - 1];
-    si[K - 1] = K - 1;
+    float cv = neutral;
+    int ci = K - 1;
 #pragma unroll
-    for (int m = K - 2; m >= 0; --m) {
-        const bool take = Op<OP>::better(sv[m + 1], v[m]);
-        sv[m] = take ? sv[m + 1] : v[m];
-        si[m] = IDX ? (take ? si[m + 1] : m) : 0;
+    for (int m = K - 1; m >= 0; --m) {
+        const bool take = Op<OP>::better_eq(v[m], cv);
+        cv = take ? v[m] : cv;
+        if (IDX) ci = take ? m : ci;
+        sv[m] = cv;
+        si[m] = ci;
     }
     emit(0, sv[0], si[0]);
-    float pv = 0.0f;
-    int pi = 0;
+    float pv = neutral;
+    int pi = K;
 #pragma unroll
     for (int m = 1; m < K; ++m) {
         const float xv = v[K + m - 1];
-        if (m == 1) {
-            pv = xv;
-            pi = K;
-        } else {
-            const bool take = Op<OP>::better(xv, pv);
-            pv = take ? xv : pv;
-            pi = IDX ? (take ? K + m - 1 : pi) : 0;
-        }
+        const bool tk = Op<OP>::better(xv, pv);
+        pv = tk ? xv : pv;
+        if (IDX) pi = tk ? K + m - 1 : pi;
         const bool take = Op<OP>::better(pv, sv[m]);
-        emit(m, take ? pv : sv[m], take ? pi - m : si[m] - m);
+        emit(m, take ? pv : sv[m], (take ? pi : si[m]) - m);
     }
-}
-
-// NaN never wins: it becomes the neutral element (max / min against the neutral element ignores a NaN
-// operand and returns every other value, -0.0 included, unchanged).
-template <int OP, typename T>
-__device__ __forceinline__ float load_clean(T v) {
-    const float f = Storage<T>::load(v);
-    return OP == kDilate ? fmaxf(f, __int_as_float(0xff800000)) : fminf(f, __int_as_float(0x7f800000));
 }
 
 // 32 mark bytes (each 0 or 1) as the bits of one word, byte i -> bit i.
@@ -112,7 +105,7 @@ __device__ __forceinline__ uint32_t pack_marks(uint4 lo, uint4 hi) {
 // after the pass, each 32-byte run of marks leaves as one word ORed into the map (words across the image
 // edge bit by bit, through the border's folding).
 template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX, int K>
-__global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
+__global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 3 : 1)) sep_sweep_fwd_kernel(const T* __restrict__ x, T* __restrict__ y,
                                                                       I* __restrict__ win, uint32_t* __restrict__ map,
                                                                       int H, int W, int border, int strips, int segs,
                                                                       int seg_h) {
@@ -195,7 +188,7 @@ __global__ void __launch_bounds__(kSweepThreads, (K <= 15 ? 4 : 1)) sep_sweep_fw
             const T* src = buf + r * XS + c * K;
             float v[2 * K - 1];
 #pragma unroll
-            for (int m = 0; m < 2 * K - 1; ++m) v[m] = load_clean<OP>(src[m]);
+            for (int m = 0; m < 2 * K - 1; ++m) v[m] = Storage<T>::load(src[m]);
             float* rvr = rv + (dst0 + r) * RS + c * K;
             uint8_t* rdr = rdj + (dst0 + r) * RS + c * K;
             sweep_run<K, OP, true>(v, [&](int m, float val, int off) {
