@@ -242,19 +242,40 @@ def _se(kind: str, C: int, dtype: torch.dtype, g: torch.Generator) -> torch.Tens
         w = torch.full((9, 13), -0.0)
         w[3:6, 4:9] = float("-inf")
         return w.to(dtype)
+    if kind == "diamond6":  # 13x13 diamond: centered flat rows of every radius (radius decomposition)
+        yy, xx = torch.meshgrid(torch.arange(13) - 6, torch.arange(13) - 6, indexing="ij")
+        return torch.where(yy.abs() + xx.abs() <= 6, 0.0, float("-inf")).to(dtype)
+    if kind == "cross9_mixed0":  # centered rows, the long one of -0.0 weights and the rest +0.0
+        w = torch.full((9, 9), float("-inf"))
+        w[:, 4] = 0.0
+        w[4, :] = -0.0
+        return w.to(dtype)
+    if kind == "ell10x9":  # even height, empty rows, centered rows of radii 0..4 out of order
+        w = torch.full((10, 9), float("-inf"))
+        for di, r in ((1, 2), (2, 4), (3, 0), (5, 3), (6, 1), (8, 4), (9, 2)):
+            w[di, 4 - r:5 + r] = 0.0
+        return w.to(dtype)
+    if kind == "disk5_shifted":  # one row off center: the whole SE walks tap by tap
+        yy, xx = torch.meshgrid(torch.arange(11) - 5, torch.arange(11) - 5, indexing="ij")
+        w = torch.where(yy * yy + xx * xx <= 25, 0.0, float("-inf"))
+        w[2] = torch.roll(w[2], 1)
+        return w.to(dtype)
     raise KeyError(kind)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16, torch.float64])
 @pytest.mark.parametrize("kind", ["rand7_perch", "rand4x6", "flat15", "flat_5x17_perch", "disk3", "flat1", "disk15",
-                                  "rand9x11", "ring9_neg0"])
+                                  "rand9x11", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted"])
 @pytest.mark.parametrize("border", [0, 1, 2])
 def test_oracle_parity_multi_tile(serron, dtype, kind, border):
     g = torch.Generator().manual_seed(hash((str(dtype), kind, border)) % (2**31))
     shape = (2, 3, 70, 133)
     x = torch.rand(*shape, generator=g).to(dtype)
-    if kind in ("flat15", "disk15", "ring9_neg0"):
+    if kind in ("flat15", "disk15", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted"):
         x = (x * 8).floor().to(dtype)  # many ties
+    if kind in ("ell10x9", "disk5_shifted"):
+        x[:, 1, 20:26, 40:47] = float("nan")  # NaN samples never win
+        x[0, 2, 0:3, :] = -x[0, 2, 0:3, :]  # signed zeros among the ties
     go = torch.randn(*shape, generator=g).to(dtype)
     w = _se(kind, shape[1], dtype, g)
     flat = bool(w.eq(0).all())
