@@ -321,6 +321,58 @@ __host__ __device__ inline size_t wide_smem(int kH, int kW, size_t acc) {
            static_cast<size_t>(kH) * 3 * sizeof(int);
 }
 
+// Keyed samples (16-bit storage, every non-empty SE row one run of one zero weight).  A staged sample
+// becomes a 32-bit key that orders like the candidates of the first-extremum rule: the value's 16 bits in
+// an order where better is smaller (-0 taken as +0, so the two compare equal as they do as floats), then
+// the SE row (added per row) and the staged column, so among equal values the first tap in raster order
+// has the smallest key; the lowest bit keeps a -0's sign for the output, below the position, where it
+// never decides.  The window's winner is then the unsigned minimum of its keys.  Neutral and NaN samples
+// (never winners) are all ones, the minimum's starting value.
+//   bits 31..16 ordered value, 15..10 SE row (kH <= 64), 9..3 staged column (< 128), 0 negative zero
+constexpr uint32_t kKeyNone = 0xffffffffu;
+constexpr int kKeyMaxRows = 64, kKeyMaxCols = 128;
+
+template <typename T>
+__device__ __forceinline__ uint32_t bits16(float f);
+template <>
+__device__ __forceinline__ uint32_t bits16<__half>(float f) {
+    return __half_as_ushort(__float2half_rn(f));
+}
+template <>
+__device__ __forceinline__ uint32_t bits16<__nv_bfloat16>(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+template <typename T>
+__device__ __forceinline__ float from_bits16(uint32_t b);
+template <>
+__device__ __forceinline__ float from_bits16<__half>(uint32_t b) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
+}
+template <>
+__device__ __forceinline__ float from_bits16<__nv_bfloat16>(uint32_t b) {
+    return __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(b)));
+}
+
+// f: a staged sample (exactly a T, NaN already replaced by the neutral element); q: its staged column
+template <typename T, int OP>
+__device__ __forceinline__ uint32_t sample_key(float f, int q) {
+    if (f == Op<OP>::template neutral<float>()) return kKeyNone;
+    uint32_t b = bits16<T>(f);
+    const uint32_t negzero = b == 0x8000u ? 1u : 0u;
+    if (negzero) b = 0u;
+    uint32_t ord = (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);  // ascending with the value
+    if (OP == kDilate) ord = ~ord & 0xffffu;                         // better = larger: descending
+    return (ord << 16) | (static_cast<uint32_t>(q) << 3) | negzero;
+}
+// the sample a key holds (its 16-bit pattern)
+template <int OP>
+__device__ __forceinline__ uint32_t key_bits16(uint32_t key) {
+    if (key & 1u) return 0x8000u;
+    uint32_t ord = key >> 16;
+    if (OP == kDilate) ord = ~ord & 0xffffu;
+    return (ord & 0x8000u) ? (ord & 0x7fffu) : (~ord & 0xffffu);
+}
+
 template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX>
 __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                        T* __restrict__ y, I* __restrict__ win, int C, int H, int W,
@@ -387,6 +439,85 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
     const int lr = 8 * (wq & 3) + (lane & 7), c0 = (4 * (wq >> 2) + (lane >> 3)) * Q;
     const int oh = oh0 + lr;
     const bool active = !(oh >= H || ow0 + c0 >= W);
+    if constexpr (sizeof(T) == 2) {
+        bool rows_ok = true;
+        for (int di = tid; di < kH; di += 256) rows_ok &= info[3 * di + 1] < info[3 * di] || info[3 * di + 2] != 0;
+        if (__syncthreads_and(rows_ok && kH <= kKeyMaxRows && cw <= kKeyMaxCols)) {
+            uint32_t* ks = reinterpret_cast<uint32_t*>(xs);  // the staged samples become keys in place
+            for (int i = tid; i < sh * cw; i += 256) {
+                const int r = i / cw, q = i - r * cw;
+                ks[r * sw + q] = sample_key<T, OP>(xs[r * sw + q], q);
+            }
+            __syncthreads();
+            if (active) {
+                uint32_t best[Q];
+#pragma unroll
+                for (int k = 0; k < Q; ++k) best[k] = kKeyNone;
+                for (int di = 0; di < kH; ++di) {
+                    const int lo = info[3 * di], hi = info[3 * di + 1];
+                    if (hi < lo) continue;
+                    const uint32_t rowbits = static_cast<uint32_t>(di) << 10;
+                    const uint32_t* row = ks + (lr + di) * sw + c0;  // output k's window starts at row[k]
+                    if (hi - lo + 1 >= Q) {
+                        // output k: suffix row[lo + k .. lo + Q - 2], core row[lo + Q - 1 .. hi], prefix
+                        // row[hi + 1 .. hi + k]
+                        uint32_t sk[Q - 1];
+                        sk[Q - 2] = row[lo + Q - 2];
+#pragma unroll
+                        for (int k = Q - 3; k >= 0; --k) sk[k] = min(row[lo + k], sk[k + 1]);
+                        uint32_t ck = row[lo + Q - 1];
+                        for (int j = lo + Q; j <= hi; ++j) ck = min(ck, row[j]);
+                        uint32_t pk = kKeyNone;
+#pragma unroll
+                        for (int k = 0; k < Q; ++k) {
+                            uint32_t rk = ck;
+                            if (k < Q - 1) rk = min(rk, sk[k]);
+                            if (k > 0) {
+                                pk = min(pk, row[hi + k]);
+                                rk = min(rk, pk);
+                            }
+                            best[k] = min(best[k], rk | rowbits);
+                        }
+                    } else {
+                        uint32_t s8[Q];
+#pragma unroll
+                        for (int k = 0; k < Q - 1; ++k) s8[k] = row[lo + k];
+                        for (int dj = lo; dj <= hi; ++dj) {
+                            s8[Q - 1] = row[dj + Q - 1];
+#pragma unroll
+                            for (int k = 0; k < Q; ++k) best[k] = min(best[k], s8[k] | rowbits);
+#pragma unroll
+                            for (int k = 0; k < Q - 1; ++k) s8[k] = s8[k + 1];
+                        }
+                    }
+                }
+                int last_winner = -1;
+                const uint32_t kw_magic = kW > 1 ? static_cast<uint32_t>(((1ull << 32) + kW - 1) / kW) : 0u;
+#pragma unroll
+                for (int k = 0; k < Q; ++k) {
+                    const int ow = ow0 + c0 + k;
+                    if (ow >= W) break;
+                    A val = neutral;
+                    int t = -1;
+                    if (best[k] != kKeyNone) {
+                        const int di = static_cast<int>((best[k] >> 10) & 63u), q = static_cast<int>((best[k] >> 3) & 127u);
+                        t = di * kW + q - (c0 + k);
+                        val = Op<OP>::tap(from_bits16<T>(key_bits16<OP>(best[k])), ws[di * kW + info[3 * di]]);
+                    }
+                    const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
+                    if (WITH_VALUE) y[o] = Storage<T>::store(val);
+                    if (WITH_INDEX) win[o] = encode_direct<I>(t);
+                    if (WITH_INDEX && map && t >= 0)
+                        marks.mark(map, tc.plane, H, W, kW, kw_magic, aH, aW, border, oh, ow, t, last_winner);
+                }
+            }
+            if (map) {
+                __syncthreads();
+                marks.flush(map, tc.plane, H, W, tid, 256);
+            }
+            return;
+        }
+    }
     if (active) {
         const bool exact = !NeedsExactCheck<T>::value || exact_flag;
         A best[Q];

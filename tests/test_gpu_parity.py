@@ -260,18 +260,20 @@ def _se(kind: str, C: int, dtype: torch.dtype, g: torch.Generator) -> torch.Tens
         w = torch.where(yy * yy + xx * xx <= 25, 0.0, float("-inf"))
         w[2] = torch.roll(w[2], 1)
         return w.to(dtype)
+    if kind == "row3x71":  # flat, wider than the 16-bit keyed form takes (128 staged columns)
+        return torch.zeros(3, 71, dtype=dtype)
     raise KeyError(kind)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16, torch.float64])
 @pytest.mark.parametrize("kind", ["rand7_perch", "rand4x6", "flat15", "flat_5x17_perch", "disk3", "flat1", "disk15",
-                                  "rand9x11", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted"])
+                                  "rand9x11", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted", "row3x71"])
 @pytest.mark.parametrize("border", [0, 1, 2])
 def test_oracle_parity_multi_tile(serron, dtype, kind, border):
     g = torch.Generator().manual_seed(hash((str(dtype), kind, border)) % (2**31))
     shape = (2, 3, 70, 133)
     x = torch.rand(*shape, generator=g).to(dtype)
-    if kind in ("flat15", "disk15", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted"):
+    if kind in ("flat15", "disk15", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted", "row3x71"):
         x = (x * 8).floor().to(dtype)  # many ties
     if kind in ("ell10x9", "disk5_shifted"):
         x[:, 1, 20:26, 40:47] = float("nan")  # NaN samples never win
