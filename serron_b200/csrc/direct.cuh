@@ -324,47 +324,46 @@ __host__ __device__ inline size_t wide_smem(int kH, int kW, size_t acc) {
 // Keyed samples (16-bit storage, every non-empty SE row one run of one zero weight).  A staged sample
 // becomes a 32-bit key that orders like the candidates of the first-extremum rule: the value's 16 bits in
 // an order where better is smaller (-0 taken as +0, so the two compare equal as they do as floats), then
-// the SE row (added per row) and the staged column, so among equal values the first tap in raster order
-// has the smallest key; the lowest bit keeps a -0's sign for the output, below the position, where it
-// never decides.  The window's winner is then the unsigned minimum of its keys.  Neutral and NaN samples
-// (never winners) are all ones, the minimum's starting value.
-//   bits 31..16 ordered value, 15..10 SE row (kH <= 64), 9..3 staged column (< 128), 0 negative zero
+// the staged row and column.  For any one output the staged row and column grow with the SE row and
+// column of the tap, so among equal values the first tap in raster order has the smallest key, and the
+// window's winner is the unsigned minimum of its keys.  The lowest bit keeps a -0's sign for the output,
+// below the position, where it never decides.  Neutral and NaN samples (never winners) are all ones, the
+// minimum's starting value; no other key has all of its low 16 bits set.
+//   bits 31..16 ordered value, 15..9 staged row (< 128), 8..2 staged column (< 128), 0 negative zero
 constexpr uint32_t kKeyNone = 0xffffffffu;
-constexpr int kKeyMaxRows = 64, kKeyMaxCols = 128;
+constexpr int kKeyMaxRows = 128, kKeyMaxCols = 128;
 
 template <typename T>
-__device__ __forceinline__ uint32_t bits16(float f);
+struct Bits16;
 template <>
-__device__ __forceinline__ uint32_t bits16<__half>(float f) {
-    return __half_as_ushort(__float2half_rn(f));
-}
+struct Bits16<__half> {
+    static constexpr uint32_t inf = 0x7c00u;
+    static __device__ __forceinline__ uint32_t of(__half v) { return __half_as_ushort(v); }
+    static __device__ __forceinline__ float value(uint32_t b) {
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
+    }
+};
 template <>
-__device__ __forceinline__ uint32_t bits16<__nv_bfloat16>(float f) {
-    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
-}
-template <typename T>
-__device__ __forceinline__ float from_bits16(uint32_t b);
-template <>
-__device__ __forceinline__ float from_bits16<__half>(uint32_t b) {
-    return __half2float(__ushort_as_half(static_cast<unsigned short>(b)));
-}
-template <>
-__device__ __forceinline__ float from_bits16<__nv_bfloat16>(uint32_t b) {
-    return __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(b)));
-}
+struct Bits16<__nv_bfloat16> {
+    static constexpr uint32_t inf = 0x7f80u;
+    static __device__ __forceinline__ uint32_t of(__nv_bfloat16 v) { return __bfloat16_as_ushort(v); }
+    static __device__ __forceinline__ float value(uint32_t b) {
+        return __bfloat162float(__ushort_as_bfloat16(static_cast<unsigned short>(b)));
+    }
+};
 
-// f: a staged sample (exactly a T, NaN already replaced by the neutral element); q: its staged column
+// b: a sample's 16-bit pattern at staged row r, column q
 template <typename T, int OP>
-__device__ __forceinline__ uint32_t sample_key(float f, int q) {
-    if (f == Op<OP>::template neutral<float>()) return kKeyNone;
-    uint32_t b = bits16<T>(f);
+__device__ __forceinline__ uint32_t sample_key(uint32_t b, int r, int q) {
+    constexpr uint32_t inf = Bits16<T>::inf, neutral = OP == kErode ? inf : (inf | 0x8000u);
+    if ((b & 0x7fffu) > inf || b == neutral) return kKeyNone;
     const uint32_t negzero = b == 0x8000u ? 1u : 0u;
     if (negzero) b = 0u;
     uint32_t ord = (b & 0x8000u) ? (~b & 0xffffu) : (b | 0x8000u);  // ascending with the value
     if (OP == kDilate) ord = ~ord & 0xffffu;                         // better = larger: descending
-    return (ord << 16) | (static_cast<uint32_t>(q) << 3) | negzero;
+    return (ord << 16) | (static_cast<uint32_t>(r) << 9) | (static_cast<uint32_t>(q) << 2) | negzero;
 }
-// the sample a key holds (its 16-bit pattern)
+// the 16-bit pattern of the sample a key holds
 template <int OP>
 __device__ __forceinline__ uint32_t key_bits16(uint32_t key) {
     if (key & 1u) return 0x8000u;
@@ -372,7 +371,6 @@ __device__ __forceinline__ uint32_t key_bits16(uint32_t key) {
     if (OP == kDilate) ord = ~ord & 0xffffu;
     return (ord & 0x8000u) ? (ord & 0x7fffu) : (~ord & 0xffffu);
 }
-
 template <typename T, int OP, typename I, bool WITH_VALUE, bool WITH_INDEX>
 __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, const T* __restrict__ w,
                                                        T* __restrict__ y, I* __restrict__ win, int C, int H, int W,
@@ -408,13 +406,6 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
         if (NeedsExactCheck<T>::value && !weight_is_exact(static_cast<float>(v))) exact_flag = 0;
     }
     const int cw = kWideCols + kW - 1;
-    for (int i = tid; i < sh * cw; i += 256) {
-        const int r = i / cw, q = i - r * cw;
-        int gr = oh0 - aH + r, gq = ow0 - aW + q;
-        A v = neutral;
-        if (resolve(gr, H, border) && resolve(gq, W, border)) v = Storage<T>::load(xp[static_cast<long long>(gr) * W + gq]);
-        xs[r * sw + q] = v != v ? neutral : v;
-    }
     __syncthreads();
     for (int di = tid; di < kH; di += 256) {
         int lo = kW, hi = -1;
@@ -431,6 +422,37 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
         info[3 * di + 1] = hi;
         info[3 * di + 2] = one ? 1 : 0;
     }
+    bool keyed = false;
+    if constexpr (sizeof(T) == 2) {
+        bool rows_ok = true;
+        for (int di = tid; di < kH; di += 256)  // rows this thread classified above
+            rows_ok &= info[3 * di + 1] < info[3 * di] || info[3 * di + 2] != 0;
+        keyed = __syncthreads_and(rows_ok && sh <= kKeyMaxRows && cw <= kKeyMaxCols);
+    } else {
+        __syncthreads();
+    }
+    if (keyed) {
+        if constexpr (sizeof(T) == 2) {
+            uint32_t* ks = reinterpret_cast<uint32_t*>(xs);
+            for (int i = tid; i < sh * cw; i += 256) {
+                const int r = i / cw, q = i - r * cw;
+                int gr = oh0 - aH + r, gq = ow0 - aW + q;
+                uint32_t key = kKeyNone;
+                if (resolve(gr, H, border) && resolve(gq, W, border))
+                    key = sample_key<T, OP>(Bits16<T>::of(xp[static_cast<long long>(gr) * W + gq]), r, q);
+                ks[r * sw + q] = key;
+            }
+        }
+    } else {
+        for (int i = tid; i < sh * cw; i += 256) {
+            const int r = i / cw, q = i - r * cw;
+            int gr = oh0 - aH + r, gq = ow0 - aW + q;
+            A v = neutral;
+            if (resolve(gr, H, border) && resolve(gq, W, border))
+                v = Storage<T>::load(xp[static_cast<long long>(gr) * W + gq]);
+            xs[r * sw + q] = v != v ? neutral : v;
+        }
+    }
     __syncthreads();
 
     // output row and first of eight columns: a warp takes 8 rows x 4 column groups, so with the odd pitch
@@ -439,84 +461,73 @@ __global__ void __launch_bounds__(256) wide_fwd_kernel(const T* __restrict__ x, 
     const int lr = 8 * (wq & 3) + (lane & 7), c0 = (4 * (wq >> 2) + (lane >> 3)) * Q;
     const int oh = oh0 + lr;
     const bool active = !(oh >= H || ow0 + c0 >= W);
-    if constexpr (sizeof(T) == 2) {
-        bool rows_ok = true;
-        for (int di = tid; di < kH; di += 256) rows_ok &= info[3 * di + 1] < info[3 * di] || info[3 * di + 2] != 0;
-        if (__syncthreads_and(rows_ok && kH <= kKeyMaxRows && cw <= kKeyMaxCols)) {
-            uint32_t* ks = reinterpret_cast<uint32_t*>(xs);  // the staged samples become keys in place
-            for (int i = tid; i < sh * cw; i += 256) {
-                const int r = i / cw, q = i - r * cw;
-                ks[r * sw + q] = sample_key<T, OP>(xs[r * sw + q], q);
-            }
-            __syncthreads();
-            if (active) {
-                uint32_t best[Q];
+    if (keyed) {
+        const uint32_t* ks = reinterpret_cast<const uint32_t*>(xs);
+        if (active) {
+            uint32_t best[Q];
 #pragma unroll
-                for (int k = 0; k < Q; ++k) best[k] = kKeyNone;
-                for (int di = 0; di < kH; ++di) {
-                    const int lo = info[3 * di], hi = info[3 * di + 1];
-                    if (hi < lo) continue;
-                    const uint32_t rowbits = static_cast<uint32_t>(di) << 10;
-                    const uint32_t* row = ks + (lr + di) * sw + c0;  // output k's window starts at row[k]
-                    if (hi - lo + 1 >= Q) {
-                        // output k: suffix row[lo + k .. lo + Q - 2], core row[lo + Q - 1 .. hi], prefix
-                        // row[hi + 1 .. hi + k]
-                        uint32_t sk[Q - 1];
-                        sk[Q - 2] = row[lo + Q - 2];
+            for (int k = 0; k < Q; ++k) best[k] = kKeyNone;
+            for (int di = 0; di < kH; ++di) {
+                const int lo = info[3 * di], hi = info[3 * di + 1];
+                if (hi < lo) continue;
+                const uint32_t* row = ks + (lr + di) * sw + c0;  // output k's window starts at row[k]
+                if (hi - lo + 1 >= Q) {
+                    // output k: suffix row[lo + k .. lo + Q - 2], core row[lo + Q - 1 .. hi], prefix
+                    // row[hi + 1 .. hi + k]
+                    uint32_t sk[Q - 1];
+                    sk[Q - 2] = row[lo + Q - 2];
 #pragma unroll
-                        for (int k = Q - 3; k >= 0; --k) sk[k] = min(row[lo + k], sk[k + 1]);
-                        uint32_t ck = row[lo + Q - 1];
-                        for (int j = lo + Q; j <= hi; ++j) ck = min(ck, row[j]);
-                        uint32_t pk = kKeyNone;
+                    for (int k = Q - 3; k >= 0; --k) sk[k] = min(row[lo + k], sk[k + 1]);
+                    uint32_t ck = row[lo + Q - 1];
+                    int j = lo + Q;
+                    for (; j < hi; j += 2) ck = __vimin3_u32(ck, row[j], row[j + 1]);
+                    if (j == hi) ck = min(ck, row[j]);
+                    best[0] = __vimin3_u32(best[0], sk[0], ck);
 #pragma unroll
-                        for (int k = 0; k < Q; ++k) {
-                            uint32_t rk = ck;
-                            if (k < Q - 1) rk = min(rk, sk[k]);
-                            if (k > 0) {
-                                pk = min(pk, row[hi + k]);
-                                rk = min(rk, pk);
-                            }
-                            best[k] = min(best[k], rk | rowbits);
-                        }
-                    } else {
-                        uint32_t s8[Q];
+                    for (int k = 1; k < Q; ++k) {
+                        ck = min(ck, row[hi + k]);  // the core and the prefix of output k
+                        best[k] = k < Q - 1 ? __vimin3_u32(best[k], sk[k], ck) : min(best[k], ck);
+                    }
+                } else {
+                    uint32_t s8[Q];
 #pragma unroll
-                        for (int k = 0; k < Q - 1; ++k) s8[k] = row[lo + k];
-                        for (int dj = lo; dj <= hi; ++dj) {
-                            s8[Q - 1] = row[dj + Q - 1];
+                    for (int k = 0; k < Q - 1; ++k) s8[k] = row[lo + k];
+                    for (int dj = lo; dj <= hi; ++dj) {
+                        s8[Q - 1] = row[dj + Q - 1];
 #pragma unroll
-                            for (int k = 0; k < Q; ++k) best[k] = min(best[k], s8[k] | rowbits);
+                        for (int k = 0; k < Q; ++k) best[k] = min(best[k], s8[k]);
 #pragma unroll
-                            for (int k = 0; k < Q - 1; ++k) s8[k] = s8[k + 1];
-                        }
+                        for (int k = 0; k < Q - 1; ++k) s8[k] = s8[k + 1];
                     }
                 }
-                int last_winner = -1;
-                const uint32_t kw_magic = kW > 1 ? static_cast<uint32_t>(((1ull << 32) + kW - 1) / kW) : 0u;
+            }
+            int last_winner = -1;
+            const uint32_t kw_magic = kW > 1 ? static_cast<uint32_t>(((1ull << 32) + kW - 1) / kW) : 0u;
 #pragma unroll
-                for (int k = 0; k < Q; ++k) {
-                    const int ow = ow0 + c0 + k;
-                    if (ow >= W) break;
-                    A val = neutral;
-                    int t = -1;
-                    if (best[k] != kKeyNone) {
-                        const int di = static_cast<int>((best[k] >> 10) & 63u), q = static_cast<int>((best[k] >> 3) & 127u);
-                        t = di * kW + q - (c0 + k);
-                        val = Op<OP>::tap(from_bits16<T>(key_bits16<OP>(best[k])), ws[di * kW + info[3 * di]]);
-                    }
-                    const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
-                    if (WITH_VALUE) y[o] = Storage<T>::store(val);
-                    if (WITH_INDEX) win[o] = encode_direct<I>(t);
-                    if (WITH_INDEX && map && t >= 0)
-                        marks.mark(map, tc.plane, H, W, kW, kw_magic, aH, aW, border, oh, ow, t, last_winner);
+            for (int k = 0; k < Q; ++k) {
+                const int ow = ow0 + c0 + k;
+                if (ow >= W) break;
+                A val = neutral;
+                int t = -1;
+                if (best[k] != kKeyNone) {
+                    const int di = static_cast<int>((best[k] >> 9) & 127u) - lr;
+                    const int dj = static_cast<int>((best[k] >> 2) & 127u) - (c0 + k);
+                    t = di * kW + dj;
+                    if constexpr (sizeof(T) == 2)
+                        val = Op<OP>::tap(Bits16<T>::value(key_bits16<OP>(best[k])), ws[di * kW + info[3 * di]]);
                 }
+                const long long o = tc.plane * H * W + static_cast<long long>(oh) * W + ow;
+                if (WITH_VALUE) y[o] = Storage<T>::store(val);
+                if (WITH_INDEX) win[o] = encode_direct<I>(t);
+                if (WITH_INDEX && map && t >= 0)
+                    marks.mark(map, tc.plane, H, W, kW, kw_magic, aH, aW, border, oh, ow, t, last_winner);
             }
-            if (map) {
-                __syncthreads();
-                marks.flush(map, tc.plane, H, W, tid, 256);
-            }
-            return;
         }
+        if (map) {
+            __syncthreads();
+            marks.flush(map, tc.plane, H, W, tid, 256);
+        }
+        return;
     }
     if (active) {
         const bool exact = !NeedsExactCheck<T>::value || exact_flag;
