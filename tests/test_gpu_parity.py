@@ -262,18 +262,27 @@ def _se(kind: str, C: int, dtype: torch.dtype, g: torch.Generator) -> torch.Tens
         return w.to(dtype)
     if kind == "row3x71":  # flat, wider than the 16-bit keyed form takes (128 staged columns)
         return torch.zeros(3, 71, dtype=dtype)
+    if kind == "rand17x17":  # two-byte records (289 taps), per-tap weights: the hashed gather walk
+        return (torch.randn(17, 17, generator=g) * 0.1).to(dtype)
+    if kind == "disk11":  # 23x23 mask, two-byte records, ties
+        yy, xx = torch.meshgrid(torch.arange(23) - 11, torch.arange(23) - 11, indexing="ij")
+        return torch.where(yy * yy + xx * xx <= 121, 0.0, float("-inf")).to(dtype)
+    if kind == "even16x18":  # even sides: the box reaches one output past the window through a fold
+        return torch.zeros(16, 18, dtype=dtype)
     raise KeyError(kind)
 
 
 @pytest.mark.parametrize("dtype", [torch.float32, torch.float16, torch.bfloat16, torch.float64])
 @pytest.mark.parametrize("kind", ["rand7_perch", "rand4x6", "flat15", "flat_5x17_perch", "disk3", "flat1", "disk15",
-                                  "rand9x11", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted", "row3x71"])
+                                  "rand9x11", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted", "row3x71",
+                                  "rand17x17", "disk11", "even16x18"])
 @pytest.mark.parametrize("border", [0, 1, 2])
 def test_oracle_parity_multi_tile(serron, dtype, kind, border):
     g = torch.Generator().manual_seed(hash((str(dtype), kind, border)) % (2**31))
     shape = (2, 3, 70, 133)
     x = torch.rand(*shape, generator=g).to(dtype)
-    if kind in ("flat15", "disk15", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted", "row3x71"):
+    if kind in ("flat15", "disk15", "ring9_neg0", "diamond6", "cross9_mixed0", "ell10x9", "disk5_shifted", "row3x71",
+                "disk11", "even16x18"):
         x = (x * 8).floor().to(dtype)  # many ties
     if kind in ("ell10x9", "disk5_shifted"):
         x[:, 1, 20:26, 40:47] = float("nan")  # NaN samples never win
